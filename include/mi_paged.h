@@ -1,0 +1,225 @@
+/*
+ * mi_paged.h -- C ABI of the B200-native paged-KV hot path of minimal-inference.
+ *
+ * One shared library (libmi_paged.so, sm_100a) exports these entry points.
+ * Every argument is a plain pointer or size: device pointers point into
+ * caller-owned CUDA memory, `stream` is a cudaStream_t (NULL = legacy default
+ * stream). Nothing here allocates device memory, synchronises the stream or
+ * reads device memory from the host, so every call can be captured into a
+ * CUDA graph.
+ *
+ * Two error channels:
+ *   - the return value (MI_OK or an MI_ERR_* code) reports argument and
+ *     launch errors found on the host; mi_last_error() gives the message;
+ *   - kernels never trap: problems found on the device (page pool exhausted,
+ *     a page id outside the pool, ...) are OR-ed as MI_STATUS_* bits into an
+ *     optional caller-owned int32 in device memory (`status`), which the
+ *     caller reads whenever it next synchronises.
+ *
+ * Page pool layout (one tensor per layer), as the reference's PagedKVCache
+ * (scheduler.py:194-202) and FlashInfer's NHD layout define it:
+ *     kv_data[num_pages][2][page_size][num_kv_heads][head_dim], K at [.][0].
+ * Page tables are CSR: kv_indptr[batch+1], kv_indices[kv_indptr[batch]],
+ * kv_last_page_len[batch]; a request with n > 0 pages holds
+ * (n-1)*page_size + last_page_len tokens, one with 0 pages holds none.
+ */
+#ifndef MI_PAGED_H
+#define MI_PAGED_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st *mi_stream_t;
+
+/* element type of q / k / v / out / the page pool */
+enum { MI_DTYPE_F32 = 0, MI_DTYPE_F16 = 1, MI_DTYPE_BF16 = 2 };
+
+/* host-side return codes */
+enum {
+  MI_OK = 0,
+  MI_ERR_INVALID = 1,     /* bad argument (shape, alignment, null pointer) */
+  MI_ERR_UNSUPPORTED = 2, /* valid but not supported by this build */
+  MI_ERR_WORKSPACE = 3,   /* workspace too small */
+  MI_ERR_CUDA = 4         /* a CUDA runtime call or launch failed */
+};
+
+/* device-side status bits (OR-ed into *status) */
+enum {
+  MI_STATUS_OUT_OF_PAGES = 1,    /* allocation larger than the free list: nothing popped */
+  MI_STATUS_BAD_PAGE = 2,        /* a page id outside [0, num_pages): access skipped */
+  MI_STATUS_BAD_POSITION = 4,    /* token position outside its pages / RoPE table: skipped */
+  MI_STATUS_BAD_BATCH_INDEX = 8, /* batch index outside [0, batch_size): skipped */
+  MI_STATUS_POOL_OVERFLOW = 16,  /* release would overfill the free list (double free) */
+  MI_STATUS_SLOT_FULL = 32,      /* a slot's page table row is full: nothing popped */
+  MI_STATUS_TIMEOUT = 64         /* a bounded device-side wait gave up: results invalid */
+};
+
+/* Message for the last non-OK return on this thread ("" if none). */
+const char *mi_last_error(void);
+/* Library ABI version (major*100 + minor). */
+int mi_version(void);
+
+/* ---------------------------------------------------------------------------
+ * (1) KV append with fused RoPE
+ *
+ * Replaces flashinfer.page.append_paged_kv_cache as model.py:207-216 calls
+ * it (flashinfer page.py:280-290; addressing page.cuh:259-283): token i of
+ * request b = batch_indices[i] at position p = positions[i] goes to page
+ * kv_indices[kv_indptr[b] + p/page_size], slot p%page_size; its K row to
+ * kv_data[page][0][slot], its V row to kv_data[page][1][slot]. Rows are
+ * [num_kv_heads][head_dim] with the given token/head strides (elements).
+ *
+ * When rope_cos/rope_sin are given ([rope_max_pos][head_dim] tables in
+ * `dtype`), K is rotated before it is stored, with the rounding of
+ * apply_rotary_emb (model.py:92-107, called at :170): bit-identical to the
+ * reference's pages. RoPE positions are rope_positions[i] (or positions[i]
+ * when NULL). When q_in is also given, the same launch writes the rotated
+ * query rows ([nnz][num_qo_heads][head_dim]) to q_out (model.py:169);
+ * q_out must not overlap q_in.
+ *
+ * A token whose page slot lies past its request's pages goes to
+ * scratch_page when scratch_page >= 0 (CUDA-graph padding lanes,
+ * scheduler.py:366-369), else it is skipped and flagged.
+ * ------------------------------------------------------------------------- */
+int mi_append_paged_kv_cache(
+    const void *append_key, int64_t k_stride_n, int64_t k_stride_h,
+    const void *append_value, int64_t v_stride_n, int64_t v_stride_h,
+    const int32_t *batch_indices, const int32_t *positions, int32_t nnz,
+    void *kv_data, int64_t num_pages, int32_t page_size, int32_t num_kv_heads,
+    int32_t head_dim, int32_t dtype,
+    const int32_t *kv_indices, const int32_t *kv_indptr, int32_t batch_size,
+    const void *rope_cos, const void *rope_sin, int32_t rope_max_pos,
+    const int32_t *rope_positions,
+    const void *q_in, int64_t q_in_stride_n, int64_t q_in_stride_h,
+    void *q_out, int64_t q_out_stride_n, int64_t q_out_stride_h, int32_t num_qo_heads,
+    int32_t scratch_page, int32_t *status, mi_stream_t stream);
+
+/* ---------------------------------------------------------------------------
+ * (2) Paged decode attention
+ *
+ * Replaces BatchDecodeWithPagedKVCacheWrapper.plan()/.run() as
+ * scheduler.py:535-539, :905-916 and model.py:224-235 use it:
+ *   out[b][h] = softmax(q[b][h] . K_b^T * sm_scale) . V_b
+ * over the kv_len tokens of request b, query head h reading KV head
+ * h / (num_qo_heads/num_kv_heads): native GQA for any group size, no head
+ * padding (model.py:227-243 pads to a power of two; not needed here).
+ * q: [batch][num_qo_heads][head_dim] with the given strides (elements);
+ * out: contiguous [batch][num_qo_heads][head_dim] in `dtype`;
+ * lse (optional): [batch][num_qo_heads] fp32, natural log. A request with
+ * no tokens gets zeros and lse = -inf.
+ *
+ * The workspace holds split-K partial results and counters. It must be
+ * zero-filled once before its first use; every call leaves its counters at
+ * zero again (after an MI_STATUS_TIMEOUT, zero-fill it again). Calls sharing
+ * a workspace must not overlap on the GPU. A page id outside the pool is
+ * flagged (MI_STATUS_BAD_PAGE) and its tokens are left out.
+ * ------------------------------------------------------------------------- */
+size_t mi_paged_decode_workspace_size(int32_t batch_size, int32_t num_qo_heads,
+                                      int32_t num_kv_heads, int32_t head_dim);
+int mi_paged_decode(
+    const void *q, int64_t q_stride_b, int64_t q_stride_h,
+    const void *kv_data, int64_t num_pages, int32_t page_size, int32_t num_kv_heads,
+    int32_t head_dim, int32_t dtype,
+    const int32_t *kv_indptr, const int32_t *kv_indices, const int32_t *kv_last_page_len,
+    int32_t batch_size, int32_t num_qo_heads, float sm_scale,
+    void *out, float *lse, void *workspace, size_t workspace_bytes, int32_t *status,
+    mi_stream_t stream);
+
+/* ---------------------------------------------------------------------------
+ * (3) Paged prefill attention
+ *
+ * Replaces BatchPrefillWithPagedKVCacheWrapper.plan()/.run() as
+ * scheduler.py:530-534, :704-716 and model.py:219-235 use it: ragged
+ * queries q[total_q][num_qo_heads][head_dim] split by qo_indptr[batch+1],
+ * attending to each request's pages (appended first). With causal != 0,
+ * query i of a request with qo_len queries and kv_len keys sees keys
+ * j <= kv_len - qo_len + i. out: contiguous [total_q][num_qo_heads][head_dim];
+ * lse optional as for decode. The workspace is reserved for split-K of long
+ * requests; pass mi_paged_prefill_workspace_size() bytes (may be 0).
+ * ------------------------------------------------------------------------- */
+size_t mi_paged_prefill_workspace_size(int32_t total_q, int32_t batch_size,
+                                       int32_t num_qo_heads, int32_t head_dim);
+int mi_paged_prefill(
+    const void *q, int64_t q_stride_n, int64_t q_stride_h,
+    const int32_t *qo_indptr, int32_t total_q,
+    const void *kv_data, int64_t num_pages, int32_t page_size, int32_t num_kv_heads,
+    int32_t head_dim, int32_t dtype,
+    const int32_t *kv_indptr, const int32_t *kv_indices, const int32_t *kv_last_page_len,
+    int32_t batch_size, int32_t num_qo_heads, int32_t causal, float sm_scale,
+    void *out, float *lse, void *workspace, size_t workspace_bytes, int32_t *status,
+    mi_stream_t stream);
+
+/* ---------------------------------------------------------------------------
+ * (4) Device page pool (replaces PagedKVCache's free list, scheduler.py:168-221)
+ *
+ * free_ring[num_pages] and pool_ctrl[4] are caller-owned device int32
+ * buffers. The pool hands out pages 0..num_pages-2 in FIFO order; page
+ * num_pages-1 is the scratch page and is never handed out (:204-206).
+ * Allocation pops from the head, release appends to the tail (:208-221), so
+ * page tables come out exactly as the reference's.
+ * ------------------------------------------------------------------------- */
+int mi_page_pool_init(int32_t *free_ring, int32_t *pool_ctrl, int32_t num_pages,
+                      mi_stream_t stream);
+/* Pop counts[0] + ... + counts[n-1] pages (all or nothing) into out_pages, in
+ * request order (PagedKVCache.allocate_pages, scheduler.py:208-214). */
+int mi_page_alloc(int32_t *free_ring, int32_t *pool_ctrl, int32_t num_pages,
+                  const int32_t *counts, int32_t n, int32_t *out_pages,
+                  int32_t *status, mi_stream_t stream);
+/* Zero pages[0..n) in every layer, then append them to the free list in order
+ * (PagedKVCache.release_pages, scheduler.py:216-221) -- one launch for all
+ * pages and layers. layer_pools: device array of num_layers pool pointers;
+ * page_bytes = 2*page_size*num_kv_heads*head_dim*elem_size. */
+int mi_page_release(int32_t *free_ring, int32_t *pool_ctrl, int32_t num_pages,
+                    const int32_t *pages, int32_t n, void *const *layer_pools,
+                    int32_t num_layers, int64_t page_bytes, int32_t *status,
+                    mi_stream_t stream);
+
+/* Slot page tables: page_table[max_slots][max_pages_per_slot] and
+ * slot_num_pages[max_slots] (device int32) hold the pages of each request
+ * slot, so a CUDA graph can grow, read and release them without the host.
+ * Slot ids outside [0, max_slots) are flagged (MI_STATUS_BAD_BATCH_INDEX) and
+ * ignored; slots listed in one call must be distinct. */
+
+/* Admission: pop counts[i] pages for slots[i], i = 0..n-1 in order
+ * (scheduler.py:624-637). All or nothing. */
+int mi_slot_alloc(int32_t *free_ring, int32_t *pool_ctrl, int32_t num_pages,
+                  int32_t *page_table, int32_t *slot_num_pages, int32_t max_slots,
+                  int32_t max_pages_per_slot,
+                  const int32_t *slots, const int32_t *counts, int32_t n,
+                  int32_t *status, mi_stream_t stream);
+/* Retire: zero and free every page of slots[0..n) in order (pages of a slot in
+ * allocation order), set their page counts to 0 (scheduler.py:984-1003). */
+int mi_slot_release(int32_t *free_ring, int32_t *pool_ctrl, int32_t num_pages,
+                    int32_t *page_table, int32_t *slot_num_pages, int32_t max_slots,
+                    int32_t max_pages_per_slot,
+                    const int32_t *slots, int32_t n, void *const *layer_pools,
+                    int32_t num_layers, int64_t page_bytes, int32_t *status,
+                    mi_stream_t stream);
+/* One decode (or prefill) step's page metadata, on the device.
+ * Lane i is request slot lane_slots[i] (-1: padding lane) whose newest token
+ * sits at lane_positions[i]. With grow != 0, a lane whose slot holds fewer
+ * than ceil((pos+1)/page_size) pages first pops the missing pages, lanes in
+ * order (scheduler.py:842-847). Then writes the CSR page table of all
+ * num_lanes lanes (scheduler.py:861-868): kv_indptr[num_lanes+1],
+ * kv_indices (capacity indices_capacity), kv_last_page_len[num_lanes], and
+ * append_positions[num_lanes] (pos, 0 for padding). Padding lanes get 0 pages
+ * and last_page_len 1 (scheduler.py:887-896); their append goes to the
+ * scratch page. */
+int mi_step_prepare(int32_t *free_ring, int32_t *pool_ctrl, int32_t num_pages,
+                    int32_t *page_table, int32_t *slot_num_pages, int32_t max_slots,
+                    int32_t max_pages_per_slot,
+                    const int32_t *lane_slots, const int32_t *lane_positions, int32_t num_lanes,
+                    int32_t page_size, int32_t grow,
+                    int32_t *kv_indptr, int32_t *kv_indices, int32_t indices_capacity,
+                    int32_t *kv_last_page_len, int32_t *append_positions,
+                    int32_t *status, mi_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MI_PAGED_H */

@@ -1,0 +1,95 @@
+"""Paged decode attention (kernel 2): drop-in for FlashInfer's decode wrapper.
+
+``BatchDecodeWithPagedKVCacheWrapper`` keeps the shape of the FlashInfer
+wrapper the reference constructs and drives (scheduler.py:535-539,
+:905-916, model.py:235): ``plan()`` records the CSR page table, ``run(q,
+kv_data)`` computes attention. ``plan()`` does no host work beyond
+validation (the kernel plans its split-K on the device), so it may run
+inside or outside a CUDA graph and never synchronises.
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+
+from . import capi
+from ._tensor import check_pool, dtype_code, need_i32, ptr, stream_of
+
+
+class BatchDecodeWithPagedKVCacheWrapper:
+    def __init__(self, float_workspace_buffer: torch.Tensor, kv_layout: str = "NHD",
+                 use_cuda_graph: bool = False, **_unused):
+        if kv_layout != "NHD":
+            raise ValueError("only the NHD layout (the reference's) is supported")
+        if not float_workspace_buffer.is_cuda:
+            raise capi.MiError("workspace must be a CUDA tensor (no CPU fallback)")
+        if float_workspace_buffer.data_ptr() % 256:
+            raise ValueError("workspace must be 256-byte aligned")
+        self._ws = float_workspace_buffer
+        # split-K counters must start at zero; every launch leaves them at zero
+        self._ws.zero_()
+        self._plan = None
+        self.status = torch.zeros(1, dtype=torch.int32, device=self._ws.device)
+
+    def plan(self, indptr: torch.Tensor, indices: torch.Tensor, last_page_len: torch.Tensor,
+             num_qo_heads: int, num_kv_heads: int, head_dim: int, page_size: int,
+             pos_encoding_mode: str = "NONE", window_left: int = -1,
+             logits_soft_cap: float | None = None, q_data_type=torch.bfloat16,
+             kv_data_type=None, data_type=None, sm_scale: float | None = None, **_unused):
+        if pos_encoding_mode != "NONE":
+            raise ValueError("only pos_encoding_mode='NONE' is supported (RoPE is applied "
+                             "by the append kernel)")
+        if window_left != -1 or logits_soft_cap not in (None, 0.0):
+            raise ValueError("sliding window / logits soft cap are not supported")
+        if num_qo_heads % num_kv_heads:
+            raise ValueError("num_qo_heads must be a multiple of num_kv_heads")
+        dev = self._ws.device
+        for name, t in (("indptr", indptr), ("indices", indices),
+                        ("last_page_len", last_page_len)):
+            need_i32(name, t, dev)
+        batch = indptr.numel() - 1
+        need = capi.lib().mi_paged_decode_workspace_size(batch, num_qo_heads, num_kv_heads,
+                                                          head_dim)
+        if need > self._ws.numel() * self._ws.element_size():
+            raise capi.MiError(f"decode workspace too small: need {need} bytes")
+        self._plan = dict(indptr=indptr, indices=indices, last=last_page_len, batch=batch,
+                          hq=num_qo_heads, hkv=num_kv_heads, d=head_dim, ps=page_size,
+                          scale=sm_scale if sm_scale is not None else 1.0 / math.sqrt(head_dim))
+
+    def run(self, q: torch.Tensor, paged_kv_cache: torch.Tensor, out: torch.Tensor | None = None,
+            lse: torch.Tensor | None = None, return_lse: bool = False):
+        """``q [B, Hq, D]`` -> ``out [B, Hq, D]`` (and ``lse [B, Hq]``)."""
+        pl = self._plan
+        if pl is None:
+            raise RuntimeError("plan() must be called before run()")
+        num_pages, ps, hkv, d = check_pool(paged_kv_cache)
+        if (ps, hkv, d) != (pl["ps"], pl["hkv"], pl["d"]):
+            raise ValueError("paged kv cache geometry differs from plan()")
+        b = pl["batch"]
+        if q.dim() != 3 or q.shape[0] < b or q.shape[1] != pl["hq"] or q.shape[2] != d:
+            raise ValueError(f"q must be [{b}, {pl['hq']}, {d}], got {tuple(q.shape)}")
+        if q.stride(-1) != 1 or q.dtype != paged_kv_cache.dtype:
+            raise ValueError("q needs the pool dtype and a unit stride on head_dim")
+        if out is None:
+            out = torch.empty((b, pl["hq"], d), dtype=q.dtype, device=q.device)
+        elif out.shape[0] < b or not out.is_contiguous() or out.dtype != q.dtype:
+            raise ValueError("out must be a contiguous [B, Hq, D] tensor of q's dtype")
+        if (return_lse or lse is not None) and lse is None:
+            lse = torch.empty((b, pl["hq"]), dtype=torch.float32, device=q.device)
+        capi.call(
+            "mi_paged_decode",
+            q.data_ptr(), q.stride(0), q.stride(1),
+            paged_kv_cache.data_ptr(), num_pages, ps, hkv, d, dtype_code(q.dtype),
+            pl["indptr"].data_ptr(), pl["indices"].data_ptr(), pl["last"].data_ptr(), b,
+            pl["hq"], pl["scale"], out.data_ptr(), ptr(lse),
+            self._ws.data_ptr(), self._ws.numel() * self._ws.element_size(),
+            self.status.data_ptr(), stream_of(q))
+        return (out, lse) if return_lse else out
+
+    def check_status(self) -> None:
+        """Synchronise and raise if a launch flagged a device-side problem."""
+        w = int(self.status.item())
+        if w:
+            self.status.zero_()
+            raise capi.MiError(f"paged decode device status: {capi.status_names(w)}")

@@ -1,0 +1,63 @@
+"""The C-ABI library loads without a GPU and exports every declared symbol."""
+import ctypes
+import os
+
+import pytest
+
+from mi_b200 import capi
+
+
+@pytest.fixture(scope="module")
+def built_lib():
+    from importlib import util
+    here = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    spec = util.spec_from_file_location(
+        "mi_build", os.path.join(here, "minimal-inference_b200", "csrc", "build.py"))
+    mod = util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    mod.build()
+    return capi.lib()
+
+
+def test_header_declares_the_hot_path():
+    syms = capi.header_symbols()
+    for name in ("mi_append_paged_kv_cache", "mi_paged_decode", "mi_paged_prefill",
+                 "mi_page_pool_init", "mi_page_alloc", "mi_page_release", "mi_slot_alloc",
+                 "mi_slot_release", "mi_step_prepare", "mi_last_error", "mi_version",
+                 "mi_paged_decode_workspace_size", "mi_paged_prefill_workspace_size"):
+        assert name in syms
+
+
+def test_library_exports_every_header_symbol(built_lib):
+    for name in capi.header_symbols():
+        assert hasattr(built_lib, name), name
+        assert name in capi._SIGS, f"{name} has no ctypes signature"
+
+
+def test_version_and_host_errors_without_gpu(built_lib):
+    assert built_lib.mi_version() >= 100
+    # argument validation happens on the host and needs no device
+    rc = built_lib.mi_page_pool_init(None, None, 0, None)
+    assert rc == 1  # MI_ERR_INVALID
+    assert b"pool_init" in built_lib.mi_last_error()
+    rc = built_lib.mi_paged_decode(None, 0, 0, None, 0, 0, 0, 0, 0, None, None, None,
+                                   1, 8, 0.1, None, None, None, 0, None, None)
+    assert rc == 1
+    assert b"decode" in built_lib.mi_last_error()
+
+
+def test_workspace_sizes(built_lib):
+    n = built_lib.mi_paged_decode_workspace_size(32, 32, 8, 128)
+    assert n > 32 * 8 * 4
+    assert built_lib.mi_paged_decode_workspace_size(0, 32, 8, 128) == 0
+
+
+def test_missing_library_fails_loudly(monkeypatch, tmp_path):
+    monkeypatch.setattr(capi, "LIB_PATH", str(tmp_path / "absent.so"))
+    monkeypatch.setattr(capi, "_lib", None)
+    with pytest.raises(capi.MiError):
+        capi.lib()
+
+
+def test_status_names():
+    assert capi.status_names(1 | 64) == ["OUT_OF_PAGES", "TIMEOUT"]
