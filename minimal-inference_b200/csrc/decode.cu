@@ -219,15 +219,16 @@ __global__ void __launch_bounds__(TcCfg<D>::NW * 32, 1) decode_tc_kernel(const D
   auto p_issue = [&](int s) {
     const int r = lane & 15, which = lane >> 4;
     const int t = p_tile * kTile + r;
-    bool valid = t < pi.kvlen;
+    bool valid = t < pi.kvlen, bad = false;
     int64_t page = 0;
     int slot = 0;
     if (valid) {
       page = p.indices[pi.page_base + t / p.ps];
       slot = t % p.ps;
-      if (page < 0 || page >= p.num_pages) valid = false;
+      if (page < 0 || page >= p.num_pages) valid = false, bad = true;
     }
     const unsigned int ball = __ballot_sync(0xffffffffu, valid);
+    if (__any_sync(0xffffffffu, bad) && lane == 0) flag(p.status, MI_STATUS_BAD_PAGE);
     if (lane == 0) {
       my_recs[s] = make_int4(p_item, p_tile, static_cast<int>(ball & 0xffffu), 0);
       mbar_arrive_expect_tx(&my_bars[s], __popc(ball) * L::ROW_BYTES);

@@ -50,11 +50,12 @@ __device__ __forceinline__ void flag(int32_t *status, int32_t bit) {
 __device__ __forceinline__ int cdiv(int a, int b) { return (a + b - 1) / b; }
 
 // Token count of request b: (n-1)*ps + last if n > 0 pages, else 0
-// (FlashInfer paged_kv_t::get_length semantics).
+// (FlashInfer paged_kv_t::get_length semantics). last is clamped to
+// [0, ps] so a malformed value can never index past the request's pages.
 __device__ __forceinline__ int kv_len_of(const int32_t *indptr, const int32_t *last, int b,
                                          int ps) {
-  int n = indptr[b + 1] - indptr[b];
-  return n > 0 ? (n - 1) * ps + last[b] : 0;
+  const int n = indptr[b + 1] - indptr[b];
+  return n > 0 ? (n - 1) * ps + min(max(last[b], 0), ps) : 0;
 }
 
 // ---------------------------------------------------------------------------
