@@ -1,0 +1,431 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 paged-KV hot path.
+
+Workload ("step"): the attention half of one Mistral-7B-shape decode step at
+BASELINE config 2 -- for each of 32 layers, one fused KV-append (RoPE on K
+and Q, scatter of the new token into its page) and one paged decode
+attention over 32 requests with contexts U[256, 4096] (seeded), 32 Q / 8 KV
+heads, head_dim 128, page_size 16, bf16, a 10240-page pool per layer with
+random non-contiguous page tables. Each layer has its own pool, so a step
+streams ~9 GB of distinct KV data (inputs far larger than the 126 MB L2).
+
+Prints ONE JSON line (rank 0): value = algorithmic GB/s of the whole job
+(all ranks' bytes / max-over-ranks device time), the decode kernel's roofline
+against the measured HBM copy bandwidth, an end-to-end figure through the
+public API with host buffers, the CPU baseline (the reference's own padded
+CPU path, ported in oracle/reference_cpu.py) and SM clocks sampled during
+the timed region.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+N > 1 runs under torchrun, one rank per GPU, each rank an independent
+replica of the workload (weak scaling; attention needs no collective).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import re
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(REPO, "minimal-inference_b200"))
+sys.path.insert(0, REPO)
+
+METRIC = "paged decode attn HBM GB/s (% of peak); Mistral-7B-shape decode tok/s @B=32"
+CFG = dict(batch=32, hq=32, hkv=8, head_dim=128, page_size=16, ctx_lo=256, ctx_hi=4096,
+           num_pages=10240, layers=32, seed=0)
+FALLBACK_HBM_GBS = 6650.0
+
+
+def config2_lens(seed=0, batch=32, lo=256, hi=4096):
+    rng = np.random.default_rng(seed)
+    return rng.integers(lo, hi + 1, size=batch).tolist()
+
+
+def decode_bytes(lens, c=CFG) -> int:
+    """Algorithmic bytes of one paged decode launch (K+V of every context
+    token, q read, out write, page ids, indptr + last_page_len)."""
+    hkv, d, hq, b = c["hkv"], c["head_dim"], c["hq"], len(lens)
+    kv = sum(lens) * hkv * d * 2 * 2
+    qo = 2 * b * hq * d * 2
+    meta = sum(math.ceil(L / c["page_size"]) for L in lens) * 4 + (2 * b + 1) * 4
+    return kv + qo + meta
+
+
+def append_bytes(b, c=CFG) -> int:
+    """Algorithmic bytes of one fused append launch (read raw q/k/v and two
+    RoPE table rows, write rotated q and the K/V rows, token metadata)."""
+    hq, hkv, d = c["hq"], c["hkv"], c["head_dim"]
+    return (b * (hq + 2 * hkv) * d * 2 + b * 2 * d * 2 + b * (hq + 2 * hkv) * d * 2
+            + b * 2 * 4)
+
+
+def read_peak():
+    p = os.path.join(REPO, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def read_traffic():
+    """DRAM bytes per decode launch from the committed ncu summary, if any."""
+    p = os.path.join(REPO, "profiles", "decode_tc_config2.md")
+    try:
+        with open(p) as f:
+            m = re.search(r"dram_bytes_per_launch:\s*([0-9.eE+]+)", f.read())
+        return float(m.group(1)) if m else None
+    except OSError:
+        return None
+
+
+# ---------------------------------------------------------------------------
+# clocks during the timed region
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        try:
+            self.p = subprocess.Popen(
+                ["nvidia-smi", f"--id={gpu_index}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=self.f, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.p = None
+        time.sleep(0.5)
+
+    def stop(self) -> dict:
+        if self.p is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.p.terminate()
+        try:
+            self.p.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.p.kill()
+        self.f.seek(0)
+        rows = [r.split(",") for r in self.f.read().strip().splitlines() if r.count(",") >= 8]
+        os.unlink(self.f.name)
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            try:
+                sm.append(float(r[1]))
+                mx.append(float(r[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, r[5:9]):
+                if v.strip() == "Active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+# CPU legs: the reference's own padded CPU path (ported in oracle/)
+# ---------------------------------------------------------------------------
+def cpu_reference_steps(lens, steps, budget_s=20.0):
+    """Time single-layer decode steps of the reference's CPU path.
+
+    Returns (GB/s of algorithmic decode bytes, seconds, threads, sample text).
+    The batch is cut to a prefix of the requests when the full batch would
+    not fit ``budget_s`` for ``steps`` steps.
+    """
+    import torch
+    from oracle.reference_cpu import PaddedDecodeLayer
+    c = CFG
+    threads = torch.get_num_threads()
+    b = len(lens)
+    layer = PaddedDecodeLayer(b, c["hkv"], c["ctx_hi"] + 1, c["head_dim"], torch.bfloat16)
+    layer.fill([L - 1 for L in lens], seed=1)
+    g = torch.Generator().manual_seed(2)
+    q = torch.randn(b, c["hq"], 1, c["head_dim"], generator=g).bfloat16()
+    kn = torch.randn(b, c["hkv"], 1, c["head_dim"], generator=g).bfloat16()
+    vn = torch.randn(b, c["hkv"], 1, c["head_dim"], generator=g).bfloat16()
+    pos = [L - 1 for L in lens]
+    t0 = time.perf_counter()
+    layer.step(list(range(b)), pos, q, kn, vn)  # warm-up + per-step estimate
+    est = time.perf_counter() - t0
+    nb = b
+    if est * steps > budget_s:
+        nb = max(1, int(b * budget_s / (est * steps)))
+    slots = list(range(nb))
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        layer.step(slots, pos[:nb], q[:nb], kn[:nb], vn[:nb])
+    dt = time.perf_counter() - t0
+    gbs = decode_bytes(lens[:nb]) * steps / dt / 1e9
+    sample = (f"{steps} single-layer decode steps of the reference CPU path (padded cache + "
+              f"SDPA, bf16) over the first {nb} of the {b} config-2 requests")
+    return gbs, dt, threads, sample
+
+
+# ---------------------------------------------------------------------------
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=300)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--layers", type=int, default=CFG["layers"],
+                    help="layer pools per step (32 = Mistral-7B; fewer only for profiling)")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    return ap.parse_args()
+
+
+def dist_env():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return rank, world, local
+
+
+def run_reference(args):
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return
+    steps, warm = max(args.steps, 1), max(args.warmup, 0)
+    lens = config2_lens(CFG["seed"])
+    # warm-up steps untimed; the timed run is bounded to ~2 minutes in total
+    if warm:
+        cpu_reference_steps(lens, warm, budget_s=20.0)  # untimed warm-up
+    gbs, dt, threads, sample = cpu_reference_steps(lens, steps, budget_s=100.0)
+    line = {
+        "metric": METRIC, "value": round(gbs, 3), "unit": "GB/s", "impl": "reference",
+        "n_gpus": args.gpus, "steps": steps, "warmup": warm,
+        "ms_per_step": round(dt / steps * 1e3, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": workload_config(),
+        "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": threads,
+                         "kind": "port", "sample": sample},
+        "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def workload_config():
+    c = CFG
+    return {"workload": "BASELINE config 2: Mistral-7B-shape paged KV append + decode "
+                        "attention, 32 layers per step, B=32, ctx U[256,4096] seeded, "
+                        "random non-contiguous page tables",
+            "model": "Mistral-7B attention shape (32 Q / 8 KV heads, head_dim 128)",
+            "global_batch": c["batch"], "seq_len": f"U[{c['ctx_lo']},{c['ctx_hi']}]",
+            "layers_per_step": c["layers"], "page_size": c["page_size"],
+            "pages_per_layer_pool": c["num_pages"], "parallelism": "replicas",
+            "l2": "inputs larger than L2: each step streams 32 distinct layer pools "
+                  "(~285 MB of KV per layer)"}
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+        return
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    from mi_b200.decode import BatchDecodeWithPagedKVCacheWrapper
+    from mi_b200.page import append_paged_kv_cache
+    from mi_b200.rope import rope_tables
+
+    rank, world, local = dist_env()
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    c = CFG
+    c["layers"] = args.layers
+    b, hq, hkv, d, ps, P, L = (c["batch"], c["hq"], c["hkv"], c["head_dim"], c["page_size"],
+                               c["num_pages"], c["layers"])
+    lens = config2_lens(c["seed"], b, c["ctx_lo"], c["ctx_hi"])
+    rng = np.random.default_rng(c["seed"])
+    perm = rng.permutation(P - 1)
+    indptr, indices, last, k0 = [0], [], [], 0
+    for n in lens:
+        np_ = math.ceil(n / ps)
+        indices.extend(perm[k0:k0 + np_].tolist())
+        k0 += np_
+        indptr.append(len(indices))
+        last.append(n % ps or ps)
+    i32 = lambda x: torch.tensor(x, dtype=torch.int32, device=dev)  # noqa: E731
+    indptr_t, indices_t, last_t = i32(indptr), i32(indices), i32(last)
+    pos_t = i32([n - 1 for n in lens])
+    bidx_t = i32(list(range(b)))
+    g = torch.Generator(device=dev).manual_seed(1234 + rank)
+    pools = [torch.randn(P, 2, ps, hkv, d, device=dev, dtype=torch.bfloat16, generator=g)
+             for _ in range(L)]
+    q_raw = torch.randn(b, hq, d, device=dev, dtype=torch.bfloat16, generator=g)
+    k_new = torch.randn(b, hkv, d, device=dev, dtype=torch.bfloat16, generator=g)
+    v_new = torch.randn(b, hkv, d, device=dev, dtype=torch.bfloat16, generator=g)
+    q_rot = torch.empty_like(q_raw)
+    out = torch.empty(b, hq, d, device=dev, dtype=torch.bfloat16)
+    cos, sin = rope_tables(d, 32768, 1e6, torch.bfloat16, dev)
+    ws = torch.zeros(128 * 1024 * 1024, dtype=torch.uint8, device=dev)
+    dec = BatchDecodeWithPagedKVCacheWrapper(ws)
+    dec.plan(indptr_t, indices_t, last_t, hq, hkv, d, ps, q_data_type=torch.bfloat16)
+
+    def layer_step(pool, ev=None):
+        """One layer through the public API (validating wrappers)."""
+        append_paged_kv_cache(k_new, v_new, bidx_t, pos_t, pool, indices_t, indptr_t, last_t,
+                              rope_cos=cos, rope_sin=sin, q=q_raw, q_out=q_rot)
+        dec.run(q_rot, pool, out=out)
+
+    # The timed loop calls the C ABI directly with arguments validated once by
+    # the calls above, so host-side Python never limits the device time.
+    from mi_b200 import capi
+    lib = capi.lib()
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    ws_bytes = ws.numel()
+    status = dec.status
+
+    def raw_args(pool):
+        app = (k_new.data_ptr(), k_new.stride(0), k_new.stride(1), v_new.data_ptr(),
+               v_new.stride(0), v_new.stride(1), bidx_t.data_ptr(), pos_t.data_ptr(), b,
+               pool.data_ptr(), P, ps, hkv, d, capi.DTYPE_BF16, indices_t.data_ptr(),
+               indptr_t.data_ptr(), b, cos.data_ptr(), sin.data_ptr(), cos.shape[0], None,
+               q_raw.data_ptr(), q_raw.stride(0), q_raw.stride(1), q_rot.data_ptr(),
+               q_rot.stride(0), q_rot.stride(1), hq, -1, status.data_ptr(), stream)
+        de = (q_rot.data_ptr(), q_rot.stride(0), q_rot.stride(1), pool.data_ptr(), P, ps, hkv,
+              d, capi.DTYPE_BF16, indptr_t.data_ptr(), indices_t.data_ptr(), last_t.data_ptr(),
+              b, hq, 1.0 / math.sqrt(d), out.data_ptr(), None, ws.data_ptr(), ws_bytes,
+              status.data_ptr(), stream)
+        return app, de
+
+    args_per_layer = [raw_args(pl) for pl in pools]
+    app_fn, dec_fn = lib.mi_append_paged_kv_cache, lib.mi_paged_decode
+
+    def raw_step(layer, ev=None):
+        app, de = args_per_layer[layer]
+        rc = app_fn(*app)
+        if ev is not None:
+            ev[0].record()
+        rc |= dec_fn(*de)
+        if ev is not None:
+            ev[1].record()
+        return rc
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    for i in range(max(args.warmup, 3)):
+        for layer in range(L):
+            layer_step(pools[layer])
+    torch.cuda.synchronize()
+    dec.check_status()
+
+    # ---- device-resident timed region ----------------------------------------
+    K = args.steps
+    nev = min(K * L, 4096)
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(nev)]
+    clocks = ClockSampler(local)
+    barrier()
+    torch.cuda.synchronize()
+    t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t_start.record()
+    n, rc = 0, 0
+    for _ in range(K):
+        for layer in range(L):
+            rc |= raw_step(layer, evs[n] if n < nev else None)
+            n += 1
+    t_end.record()
+    if rc:
+        raise capi.MiError(f"launch failed in the timed loop: {lib.mi_last_error().decode()}")
+    torch.cuda.synchronize()
+    barrier()
+    clk = clocks.stop()
+    ms_total = max_over_ranks(t_start.elapsed_time(t_end))
+    dec_ms = statistics.mean(a.elapsed_time(bb) for a, bb in evs)
+    dec.check_status()
+
+    step_bytes = L * (decode_bytes(lens) + append_bytes(b))
+    ms_per_step = ms_total / K
+    value = world * step_bytes * K / (ms_total / 1e3) / 1e9
+    peak, peak_kind = read_peak()
+    achieved = decode_bytes(lens) / (dec_ms / 1e3) / 1e9
+    traffic = read_traffic()
+
+    # ---- end to end through the public API with host buffers -----------------
+    e2e = None
+    if not args.no_e2e:
+        q_h = torch.randn(L, b, hq, d, dtype=torch.bfloat16).pin_memory()
+        k_h = torch.randn(L, b, hkv, d, dtype=torch.bfloat16).pin_memory()
+        v_h = torch.randn(L, b, hkv, d, dtype=torch.bfloat16).pin_memory()
+        o_h = torch.empty(L, b, hq, d, dtype=torch.bfloat16).pin_memory()
+        ke = max(1, min(K, 50))
+        barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(ke):
+            for layer in range(L):
+                q_raw.copy_(q_h[layer], non_blocking=True)
+                k_new.copy_(k_h[layer], non_blocking=True)
+                v_new.copy_(v_h[layer], non_blocking=True)
+                layer_step(pools[layer])
+                o_h[layer].copy_(out, non_blocking=True)
+            torch.cuda.current_stream().synchronize()  # the caller reads this step's result
+        e1.record()
+        torch.cuda.synchronize()
+        barrier()
+        e2e_ms = max_over_ranks(e0.elapsed_time(e1)) / ke
+        e2e = {"value": round(world * step_bytes / (e2e_ms / 1e3) / 1e9, 2), "unit": "GB/s",
+               "ms_per_step": round(e2e_ms, 4),
+               "h2d_bytes_per_step": L * b * (hq + 2 * hkv) * d * 2,
+               "d2h_bytes_per_step": L * b * hq * d * 2}
+
+    # ---- CPU baseline (rank 0, N = 1 only) ------------------------------------
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        gbs, _, threads, sample = cpu_reference_steps(lens, 8, budget_s=20.0)
+        cpu = {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+               "sample": sample}
+
+    if world > 1:
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
+        "steps": K, "warmup": max(args.warmup, 3), "ms_per_step": round(ms_per_step, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic", "config": workload_config(),
+        "roofline": {"bound": "hbm", "kernel": "decode_tc_kernel",
+                     "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
+                     "traffic": traffic, "algorithmic_bytes": decode_bytes(lens),
+                     "avg_launch_us": round(dec_ms * 1e3, 2)},
+        "cpu_baseline": cpu, "e2e": e2e, "clocks": clk,
+        "gpu_launches": 2 * K * L,
+    }
+    print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()
