@@ -130,6 +130,37 @@ int mi_paged_decode(
     mi_stream_t stream);
 
 /* ---------------------------------------------------------------------------
+ * Paged decode for callers that cannot allocate device memory.
+ *
+ * No counterpart in the reference. Some hosts manage all GPU memory through
+ * their own allocator (a serving runtime's caching pool, a fixed arena given
+ * to plugins) and offer a kernel library no way to get a workspace; others
+ * call from places where cudaMalloc is not allowed or would stall the
+ * device. This variant of mi_paged_decode takes the same arguments minus the
+ * workspace and allocates nothing: its split-K scratch is a fixed array of
+ * MI_DECODE_STATIC_SCRATCH_BYTES inside the library, which every GPU that
+ * loads the library holds until the process exits. The caller still passes
+ * q, the pool, the page tables and out.
+ *   - Limit: batch_size * num_kv_heads counters plus one partial slot per
+ *     (request, KV head) of group*head_dim*4 bytes must fit in the array;
+ *     larger calls return MI_ERR_WORKSPACE and launch nothing.
+ *   - All calls share the array. Each call first clears its counters on
+ *     `stream`; calls that overlap on the GPU (other streams, unordered
+ *     threads) race on the array and must be serialised by the caller.
+ *   - The first call on each device looks up the array's device address
+ *     (once per device, with that device current); make that first call
+ *     before any stream capture.
+ * ------------------------------------------------------------------------- */
+#define MI_DECODE_STATIC_SCRATCH_BYTES (8u << 20)
+int mi_paged_decode_noalloc(
+    const void *q, int64_t q_stride_b, int64_t q_stride_h,
+    const void *kv_data, int64_t num_pages, int32_t page_size, int32_t num_kv_heads,
+    int32_t head_dim, int32_t dtype,
+    const int32_t *kv_indptr, const int32_t *kv_indices, const int32_t *kv_last_page_len,
+    int32_t batch_size, int32_t num_qo_heads, float sm_scale,
+    void *out, float *lse, int32_t *status, mi_stream_t stream);
+
+/* ---------------------------------------------------------------------------
  * (3) Paged prefill attention
  *
  * Replaces BatchPrefillWithPagedKVCacheWrapper.plan()/.run() as

@@ -28,6 +28,8 @@
 // (request, query head), warps split the tokens, online softmax per warp,
 // merged through shared memory. Used for fp32 parity configs and shapes the
 // fast path does not cover.
+#include <mutex>
+
 #include "mi_common.cuh"
 
 namespace mi {
@@ -700,4 +702,90 @@ extern "C" int mi_paged_decode(
     case MI_DTYPE_F16: return launch_generic<__half>(p, s);
     default: return launch_generic<__nv_bfloat16>(p, s);
   }
+}
+
+// ---------------------------------------------------------------------------
+// Paged decode for callers that cannot allocate device memory.
+//
+// Some hosts own every byte of GPU memory through their own allocator (a
+// serving runtime's caching pool, a fixed arena handed to plugins) and give a
+// kernel library no way to obtain a workspace; others call in from places
+// where a cudaMalloc is not allowed or would stall the whole device. For them
+// the split-K scratch lives in a fixed array inside this library instead of a
+// caller-provided workspace. Every GPU that loads the library holds the array
+// until the process exits.
+// ---------------------------------------------------------------------------
+namespace mi {
+
+static __device__ __align__(256) unsigned char g_decode_scratch[MI_DECODE_STATIC_SCRATCH_BYTES];
+
+namespace {
+
+constexpr int kMaxScratchDevices = 64;
+std::mutex g_scratch_mu;
+void *g_scratch_addr[kMaxScratchDevices] = {};
+
+// Device address of g_decode_scratch on the current device. Looked up once
+// per device (with that device current) and cached; in host code the array's
+// name is only a stand-in, never a usable pointer.
+int scratch_address(void **out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess)
+    return fail(MI_ERR_CUDA, "decode_noalloc: cudaGetDevice: %s", cudaGetErrorString(e));
+  if (dev < 0 || dev >= kMaxScratchDevices)
+    return fail(MI_ERR_UNSUPPORTED, "decode_noalloc: device %d beyond %d", dev,
+                kMaxScratchDevices);
+  std::lock_guard<std::mutex> lock(g_scratch_mu);
+  if (g_scratch_addr[dev] == nullptr) {
+    void *p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_decode_scratch);
+    if (e != cudaSuccess || p == nullptr)
+      return fail(MI_ERR_CUDA, "decode_noalloc: cudaGetSymbolAddress: %s",
+                  cudaGetErrorString(e));
+    g_scratch_addr[dev] = p;
+  }
+  *out = g_scratch_addr[dev];
+  return MI_OK;
+}
+
+}  // namespace
+}  // namespace mi
+
+extern "C" int mi_paged_decode_noalloc(
+    const void *q, int64_t q_stride_b, int64_t q_stride_h,
+    const void *kv_data, int64_t num_pages, int32_t page_size, int32_t num_kv_heads,
+    int32_t head_dim, int32_t dtype,
+    const int32_t *kv_indptr, const int32_t *kv_indices, const int32_t *kv_last_page_len,
+    int32_t batch_size, int32_t num_qo_heads, float sm_scale,
+    void *out, float *lse, int32_t *status, mi_stream_t stream) {
+  using namespace mi;
+  MI_REQUIRE(batch_size >= 0, "decode_noalloc: negative batch_size");
+  if (batch_size == 0) return MI_OK;
+  MI_REQUIRE(num_kv_heads > 0 && head_dim > 0 && num_qo_heads >= num_kv_heads &&
+                 num_qo_heads % num_kv_heads == 0,
+             "decode_noalloc: bad head counts %d / %d", num_qo_heads, num_kv_heads);
+  // Room for the counters plus at least one partial slot per (request, KV
+  // head); anything larger than the fixed array is refused here.
+  const size_t group = static_cast<size_t>(num_qo_heads / num_kv_heads);
+  const size_t counters = kCtrlBytes + align256(size_t(batch_size) * num_kv_heads * 4);
+  const size_t per_item = group * head_dim * 4 + group * 4;
+  const size_t need = counters + 512 + (size_t(batch_size) * num_kv_heads + 1) * per_item;
+  if (need > MI_DECODE_STATIC_SCRATCH_BYTES)
+    return fail(MI_ERR_WORKSPACE,
+                "decode_noalloc: batch %d x %d KV heads needs %zu bytes of scratch, more than "
+                "the library's fixed %u bytes; use mi_paged_decode with a workspace",
+                batch_size, num_kv_heads, need, (unsigned)MI_DECODE_STATIC_SCRATCH_BYTES);
+  void *scratch = nullptr;
+  int rc = scratch_address(&scratch);
+  if (rc != MI_OK) return rc;
+  // The array keeps the previous call's contents: clear the counters the
+  // kernel expects at zero (partial slots are written before they are read).
+  cudaError_t e = cudaMemsetAsync(scratch, 0, counters, reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess)
+    return fail(MI_ERR_CUDA, "decode_noalloc: clearing scratch: %s", cudaGetErrorString(e));
+  return mi_paged_decode(q, q_stride_b, q_stride_h, kv_data, num_pages, page_size, num_kv_heads,
+                         head_dim, dtype, kv_indptr, kv_indices, kv_last_page_len, batch_size,
+                         num_qo_heads, sm_scale, out, lse, scratch,
+                         MI_DECODE_STATIC_SCRATCH_BYTES, status, stream);
 }

@@ -48,6 +48,11 @@ _SIGS = {
         _c_p, _c_i64, _c_i32, _c_i32, _c_i32, _c_i32,
         _c_p, _c_p, _c_p, _c_i32, _c_i32, _c_f,
         _c_p, _c_p, _c_p, _c_size, _c_p, _c_p], ctypes.c_int),
+    "mi_paged_decode_noalloc": ([
+        _c_p, _c_i64, _c_i64,
+        _c_p, _c_i64, _c_i32, _c_i32, _c_i32, _c_i32,
+        _c_p, _c_p, _c_p, _c_i32, _c_i32, _c_f,
+        _c_p, _c_p, _c_p, _c_p], ctypes.c_int),
     "mi_paged_prefill_workspace_size": ([_c_i32, _c_i32, _c_i32, _c_i32], _c_size),
     "mi_paged_prefill": ([
         _c_p, _c_i64, _c_i64, _c_p, _c_i32,
