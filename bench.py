@@ -416,7 +416,7 @@ def main():
         "steps": K, "warmup": max(args.warmup, 3), "ms_per_step": round(ms_per_step, 4),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic", "config": workload_config(),
-        "roofline": {"bound": "hbm", "kernel": "decode_tc_kernel",
+        "roofline": {"bound": "hbm", "kernel": "decode_sk_kernel",
                      "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
                      "traffic": traffic, "algorithmic_bytes": decode_bytes(lens),

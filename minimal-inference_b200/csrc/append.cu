@@ -110,6 +110,8 @@ __device__ __forceinline__ void rope_chunk(float (&out)[VEC], const T *row, int 
 
 template <typename T, int VEC>
 __global__ void __launch_bounds__(256) append_kernel(const AppendParams p) {
+  pdl_wait();     // predecessors' writes (q/k/v producers, readers of q_out) are done
+  pdl_trigger();  // the attention kernel that follows may get scheduled now
   const int nchunk = p.d / VEC;
   const int nq = p.q_in ? p.hq * nchunk : 0;
   const int nk = p.hkv * nchunk;
@@ -188,10 +190,9 @@ int launch_append(const AppendParams &p, bool vec_ok, cudaStream_t stream) {
   int gy = (items + threads - 1) / threads;
   int gx = p.nnz < (1 << 20) ? p.nnz : (1 << 20);
   dim3 grid(gx, gy);
-  if (vec_ok)
-    append_kernel<T, V16><<<grid, threads, 0, stream>>>(p);
-  else
-    append_kernel<T, 1><<<grid, threads, 0, stream>>>(p);
+  cudaError_t e = vec_ok ? launch_pdl(append_kernel<T, V16>, grid, dim3(threads), 0, stream, p)
+                         : launch_pdl(append_kernel<T, 1>, grid, dim3(threads), 0, stream, p);
+  if (e != cudaSuccess) return fail(MI_ERR_CUDA, "append_kernel launch: %s", cudaGetErrorString(e));
   return check_launch("append_kernel");
 }
 

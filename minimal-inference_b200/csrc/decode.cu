@@ -30,6 +30,7 @@
 // fast path does not cover.
 #include <mutex>
 
+#include "decode_sk.cuh"
 #include "mi_common.cuh"
 
 namespace mi {
@@ -639,8 +640,10 @@ extern "C" size_t mi_paged_decode_workspace_size(int32_t batch_size, int32_t num
   using namespace mi;
   if (batch_size <= 0 || num_kv_heads <= 0 || num_qo_heads < num_kv_heads || head_dim <= 0)
     return 0;
-  return fast_ws_bytes(batch_size, num_qo_heads, num_kv_heads, head_dim,
-                       fast_max_items(batch_size, num_kv_heads)) + 512;
+  const size_t v1 = fast_ws_bytes(batch_size, num_qo_heads, num_kv_heads, head_dim,
+                                 fast_max_items(batch_size, num_kv_heads)) + 512;
+  const size_t sk = decode_sk_workspace_bytes(batch_size, num_qo_heads, num_kv_heads, head_dim);
+  return v1 > sk ? v1 : sk;
 }
 
 extern "C" int mi_paged_decode(
@@ -694,6 +697,12 @@ extern "C" int mi_paged_decode(
   if (fast) {
     MI_REQUIRE(reinterpret_cast<uintptr_t>(workspace) % 256 == 0,
                "decode: workspace must be 256-byte aligned");
+    // stream-K TMA kernel first; the persistent ticket kernel covers the rest
+    SkArgs sk{q, q_stride_b, q_stride_h, kv_data, num_pages, page_size, num_kv_heads,
+              head_dim, dtype, kv_indptr, kv_indices, kv_last_page_len, batch_size,
+              num_qo_heads, sm_scale, out, lse, workspace, workspace_bytes, status, s};
+    const int rc = launch_decode_sk(sk);
+    if (rc >= 0) return rc;
     return dtype == MI_DTYPE_BF16 ? launch_fast<__nv_bfloat16>(p, workspace, workspace_bytes, s)
                                   : launch_fast<__half>(p, workspace, workspace_bytes, s);
   }

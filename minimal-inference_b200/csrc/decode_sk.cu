@@ -1,0 +1,735 @@
+// Kernel (2), stream-K version: paged decode attention fed by TMA tensor loads.
+//
+// Same contract as decode.cu (FlashInfer BatchDecodeWithPagedKVCacheWrapper
+// as scheduler.py:535-539, :905-916 and model.py:235 use it), for the shapes
+// the reference serves: bf16/fp16, head_dim 64/128, page_size a multiple of
+// 16, 1/2/4/8 KV heads, GQA group <= 16.
+//
+// Work split ("stream-K"): the requests' pages, concatenated in kv_indices
+// order, are cut into gridDim.x equal runs of T = ceil(total/grid) pages;
+// CTA i streams run i. A request wholly inside one run is finished there;
+// one cut by run boundaries gets a normalised partial per run (slot
+// blockIdx.x + b), which a second, fully parallel kernel merges (one warp
+// per request and query head). Merging in the decode kernel itself put every
+// merge at the very end of the runs, serialised behind the last arrivals.
+// Both kernels derive T from kv_indptr on the device, so the launches need
+// no host plan() and can be graph-captured.
+//
+// CTA = 1 producer warp + 8 consumer warps.
+//   * Producer: walks its run 16 tokens ("tile") at a time. Page ids come
+//     from coalesced 32-wide windows of kv_indices held in registers (the
+//     next window is prefetched). For each tile it waits for a free stage,
+//     writes the stage record, and its lanes issue one 4-D TMA tensor load
+//     (cp.async.bulk.tensor, SWIZZLE_128B) per (K/V, 64-wide half of
+//     head_dim, KV head): a 16-token x 128-byte box. The stage's mbarrier
+//     counts the bytes.
+//   * Consumers: warp w serves KV head w / (8/Hkv) and takes every
+//     (8/Hkv)-th tile of a run segment. The group's query heads are the M
+//     rows of mma.sync m16n8k16 (S = Q K^T, O += P V, P in registers), online
+//     softmax in the exp2 domain. The 128-byte swizzle puts the 8 rows of
+//     every ldmatrix in different banks.
+//   * Warps sharing a KV head combine through shared memory (bounded
+//     mbarrier sync); all cross-warp waits are bounded, so nothing can hang.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "mi_common.cuh"
+
+#include "decode_sk.cuh"
+
+namespace mi {
+namespace {
+
+constexpr int kNC = 8;                    // consumer warps
+constexpr int kThreads = (kNC + 1) * 32;  // + one producer warp
+constexpr int kTile = 16;
+constexpr int kMaxStages = 8;
+constexpr int kSmemLimit = 232448;        // 227 KB opt-in per CTA
+constexpr size_t kCtrl = 256;
+
+inline size_t al256(size_t x) { return (x + 255) & ~size_t(255); }
+
+struct SkParams {
+  const void *q;
+  int64_t qsb, qsh;
+  int64_t num_pages;
+  int ps, hkv, group, hq, batch, subs, stages, stage_bytes;
+  const int32_t *indptr, *indices, *last;
+  float scale_log2;
+  void *out;
+  float *lse;
+  int32_t *status;
+  unsigned *arrive;  // [batch * hkv] (reserved; the merge kernel needs no counters)
+  float *part_o;     // [(grid + batch)][hq][D]
+  float *part_lse;   // [(grid + batch)][hq]
+  int bar_off, rec_off, scr_off, scr_bufs;
+  int meta_off;  // >= 0: kv_indptr / kv_last_page_len staged in shared memory here
+};
+
+constexpr int kSmemBatch = 1024;  // requests whose metadata fits the shared-memory copy
+
+struct __align__(16) StageRec {
+  int b, tok0, kvlen, flags;  // flags: 1 first, 2 last, 4 direct, 8 bad page; ordinal << 8
+};
+
+__device__ __forceinline__ void tma_load_4d(void *dst, const CUtensorMap *map, int c0, int c1,
+                                            int c2, int c3, uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3),
+      "r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// Offset of 16-byte chunk `c` of row `r` in a 128-byte-swizzled box.
+__device__ __forceinline__ uint32_t swz(int r, int c) {
+  return static_cast<uint32_t>(r * 128 + ((c ^ (r & 7)) << 4));
+}
+
+template <typename T, int D, bool G16>
+__global__ void __launch_bounds__(kThreads, 1)
+    decode_sk_kernel(const __grid_constant__ CUtensorMap tmap, const SkParams p) {
+  constexpr int KS = D / 16, NT = D / 8, DH = D / 64;
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char *smem = reinterpret_cast<unsigned char *>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int S = p.stages;
+  uint64_t *full = reinterpret_cast<uint64_t *>(smem + p.bar_off);
+  uint64_t *empty = full + kMaxStages;
+  uint64_t *hsync = empty + kMaxStages;  // [hkv]
+  StageRec *recs = reinterpret_cast<StageRec *>(smem + p.rec_off);
+  float *scratch = reinterpret_cast<float *>(smem + p.scr_off);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int G = gridDim.x, cta = blockIdx.x;
+
+  if (threadIdx.x < S) {
+    mbar_init(&full[threadIdx.x], 1);
+    mbar_init(&empty[threadIdx.x], kNC);
+  }
+  if (threadIdx.x >= 32 && threadIdx.x < 32 + p.hkv) mbar_init(&hsync[threadIdx.x - 32], p.subs);
+  pdl_trigger();  // the merge kernel may get scheduled next to this grid
+  pdl_wait();     // the append that wrote this step's K/V and q has finished
+  // The producer's first page-id window only needs this CTA's run start, so
+  // its loads go out together with the metadata staging below.
+  int pre_pw = -1, pre_pwn = -1;
+  if (warp == kNC) {
+    if (lane == 0)
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap)) : "memory");
+    const int b0 = p.indptr[0], tot = p.indptr[p.batch] - b0;
+    const int lo0 = blockIdx.x * (tot > 0 ? cdiv(tot, gridDim.x) : 1);
+    pre_pw = (lo0 + lane < tot) ? p.indices[b0 + lo0 + lane] : -1;
+    pre_pwn = (lo0 + 32 + lane < tot) ? p.indices[b0 + lo0 + 32 + lane] : -1;
+  }
+  // per-request metadata, read many times below: one coalesced copy to smem
+  const int32_t *ip = p.indptr, *lp = p.last;
+  if (p.meta_off >= 0) {
+    int32_t *s_ip = reinterpret_cast<int32_t *>(smem + p.meta_off);
+    int32_t *s_lp = s_ip + kSmemBatch + 1;
+    for (int i = threadIdx.x; i <= p.batch; i += blockDim.x) {
+      s_ip[i] = p.indptr[i];
+      if (i < p.batch) s_lp[i] = p.last[i];
+    }
+    ip = s_ip;
+    lp = s_lp;
+  }
+  fence_mbar_init();
+  __syncthreads();
+  const int base0 = ip[0];
+  const int total = ip[p.batch] - base0;
+  const int run = total > 0 ? cdiv(total, G) : 1;  // pages per CTA
+
+  const int block_bytes = p.hkv * kTile * 128;  // one (K/V, d-half) block of a stage
+
+  // =========================== producer warp ==============================
+  if (warp == kNC) {
+    int k = 0;
+    bool ok_run = true;
+    const int lo = cta * run, hi = min(total, lo + run);
+    if (lo < hi) {
+      int b = 0;
+      {  // request holding global page position lo: last b with indptr[b]-base0 <= lo
+        int l = 0, h = p.batch - 1;
+        while (l < h) {
+          const int mid = (l + h + 1) >> 1;
+          if (ip[mid] - base0 <= lo) l = mid; else h = mid - 1;
+        }
+        b = l;
+      }
+      int wbase = lo;
+      int pw = pre_pw, pwn = pre_pwn;  // loaded during the prologue
+      for (int pos = lo; pos < hi && ok_run;) {
+        while (ip[b + 1] - base0 <= pos) ++b;
+        const int start_b = ip[b] - base0, end_b = ip[b + 1] - base0;
+        const int kvlen = kv_len_of(ip, lp, b, p.ps);
+        const int sub_hi = min(hi, end_b);
+        const bool direct = start_b >= lo && end_b <= hi;
+        const int tok_begin = (pos - start_b) * p.ps;
+        const int tok_end = min(kvlen, (sub_hi - start_b) * p.ps);
+        // A segment without tokens (last_page_len 0) still gets one fully
+        // masked tile, so its partial and its merge arrival exist.
+        const int ntiles = tok_end > tok_begin ? cdiv(tok_end - tok_begin, kTile) : 1;
+        for (int j = 0; j < ntiles; ++j) {
+          const int tok0 = tok_begin + j * kTile;
+          const int gpos = start_b + tok0 / p.ps;
+          while (gpos >= wbase + 32) {
+            wbase += 32;
+            pw = pwn;
+            pwn = (wbase + 32 + lane < total) ? p.indices[base0 + wbase + 32 + lane] : -1;
+          }
+          const int page = __shfl_sync(0xffffffffu, pw, gpos - wbase);
+          const bool bad = page < 0 || page >= p.num_pages;
+          const int s = k % S;
+          if (!mbar_wait_bounded(&empty[s], ((k / S) & 1) ^ 1)) {
+            ok_run = false;
+            break;
+          }
+          int flags = (j == 0 ? 1 : 0) | (j == ntiles - 1 ? 2 : 0) | (direct ? 4 : 0) |
+                      (bad ? 8 : 0) | (j << 8);
+          if (lane == 0) {
+            recs[s] = StageRec{b, tok0, kvlen, flags};
+            mbar_arrive_expect_tx(&full[s], bad ? 0u : static_cast<uint32_t>(p.stage_bytes));
+            if (bad) flag(p.status, MI_STATUS_BAD_PAGE);
+          }
+          __syncwarp();
+          if (!bad) {
+            // lane -> (kv, d-half, head)
+            const int nbox = 2 * DH * p.hkv;
+            if (lane < nbox) {
+              const int h = lane % p.hkv, rest = lane / p.hkv;
+              const int dh = rest % DH, which = rest / DH;
+              unsigned char *dst = smem + s * p.stage_bytes + (which * DH + dh) * block_bytes +
+                                   h * (kTile * 128);
+              tma_load_4d(dst, &tmap, dh * 64, h, tok0 % p.ps, page * 2 + which, &full[s]);
+            }
+          }
+          ++k;
+        }
+        pos = sub_hi;
+      }
+    }
+    // end-of-run sentinel
+    bool sentinel = false;
+    if (ok_run) {
+      const int s = k % S;
+      if (mbar_wait_bounded(&empty[s], ((k / S) & 1) ^ 1)) {
+        if (lane == 0) {
+          recs[s] = StageRec{-1, 0, 0, 0};
+          mbar_arrive(&full[s]);
+        }
+        sentinel = true;
+      } else {
+        ok_run = false;
+      }
+    }
+    // No copy may still be in flight when the CTA retires. The sentinel
+    // reused stage k % S, whose copy (issue k - S) had landed before its
+    // consumers released it, so only the later issues need a wait.
+    for (int kk = max(0, sentinel ? k - S + 1 : k - S); kk < k; ++kk)
+      if (!mbar_wait_bounded(&full[kk % S], (kk / S) & 1)) ok_run = false;
+    if (!ok_run && lane == 0) flag(p.status, MI_STATUS_TIMEOUT);
+    return;
+  }
+
+  // =========================== consumer warps =============================
+  const int subs = p.subs;
+  const int h = warp / subs, sw = warp % subs;
+  const int gid = lane >> 2, tq = lane & 3;
+
+  // requests with no tokens: zeros, lse = -inf
+  for (int b = cta * kNC + warp; b < p.batch; b += G * kNC) {
+    if (kv_len_of(ip, lp, b, p.ps) != 0) continue;
+    T *o = static_cast<T *>(p.out) + static_cast<int64_t>(b) * p.hq * D;
+    for (int i = lane; i < p.hq * D; i += 32) o[i] = Elt<T>::from(0.f);
+    if (p.lse)
+      for (int i = lane; i < p.hq; i += 32) p.lse[b * p.hq + i] = -INFINITY;
+  }
+
+  uint32_t qa[KS][4];
+  float o[NT][4];
+  float m0 = -INFINITY, l0 = 0.f, m1 = -INFINITY, l1 = 0.f;
+  int segments = 0;
+  bool timed_out = false;
+
+  for (int k = 0;; ++k) {
+    const int s = k % S;
+    if (!mbar_wait_bounded(&full[s], (k / S) & 1)) {
+      timed_out = true;
+      break;
+    }
+    const StageRec rec = recs[s];
+    if (rec.b < 0) break;
+    const int flags = rec.flags;
+    if (flags & 1) {  // first tile of a run segment: this warp's query rows
+      const T *qb = static_cast<const T *>(p.q) + static_cast<int64_t>(rec.b) * p.qsb;
+      const int r0 = h * p.group + gid;
+#pragma unroll
+      for (int kk = 0; kk < KS; ++kk) {
+        const int dc = kk * 16 + 2 * tq;
+        uint32_t a0 = 0, a1 = 0, a2 = 0, a3 = 0;
+        if (gid < p.group) {
+          const T *qr = qb + static_cast<int64_t>(r0) * p.qsh;
+          a0 = *reinterpret_cast<const uint32_t *>(qr + dc);
+          a2 = *reinterpret_cast<const uint32_t *>(qr + dc + 8);
+        }
+        if (G16 && gid + 8 < p.group) {
+          const T *qr = qb + static_cast<int64_t>(r0 + 8) * p.qsh;
+          a1 = *reinterpret_cast<const uint32_t *>(qr + dc);
+          a3 = *reinterpret_cast<const uint32_t *>(qr + dc + 8);
+        }
+        qa[kk][0] = a0;
+        qa[kk][1] = a1;
+        qa[kk][2] = a2;
+        qa[kk][3] = a3;
+      }
+#pragma unroll
+      for (int n = 0; n < NT; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+      m0 = m1 = -INFINITY;
+      l0 = l1 = 0.f;
+    }
+    if (((flags >> 8) % subs) == sw) {
+      unsigned char *st = smem + s * p.stage_bytes;
+      const uint32_t kbase = smem_u32(st) + h * (kTile * 128);
+      const uint32_t vbase = kbase + DH * block_bytes;
+      const int nvalid = (flags & 8) ? 0 : rec.kvlen - rec.tok0;
+      if (nvalid < kTile) {
+        // rows past the request (or of a bad page) may hold anything: zero
+        // this head's V rows there so P = 0 never meets a NaN
+        const int rows = kTile - max(nvalid, 0);
+        unsigned char *vrow = st + DH * block_bytes + h * (kTile * 128);
+        for (int idx = lane; idx < rows * 8 * DH; idx += 32) {
+          const int dh = idx / (rows * 8), rem = idx % (rows * 8);
+          const int r = max(nvalid, 0) + rem / 8, c = rem % 8;
+          *reinterpret_cast<uint4 *>(vrow + dh * block_bytes + r * 128 + c * 16) =
+              make_uint4(0, 0, 0, 0);
+        }
+        __syncwarp();
+        fence_proxy_async_smem();
+      }
+      float s0[4] = {0.f, 0.f, 0.f, 0.f}, s1[4] = {0.f, 0.f, 0.f, 0.f};
+      {
+        // even / odd k-steps accumulate separately: two MMA chains per n-tile
+        float e0[4] = {0.f, 0.f, 0.f, 0.f}, e1[4] = {0.f, 0.f, 0.f, 0.f};
+        const int mi = lane >> 3;
+        const int rk = ((mi >> 1) << 3) + (lane & 7);  // token row of this lane's address
+#pragma unroll
+        for (int kk = 0; kk < KS; ++kk) {
+          const int c = ((kk & 3) << 1) + (mi & 1);
+          uint32_t b0, b1, b2, b3;
+          ldsm_x4(b0, b1, b2, b3, kbase + (kk >> 2) * block_bytes + swz(rk, c));
+          if (kk & 1) {
+            Mma<T>::run(e0, qa[kk], b0, b1);
+            Mma<T>::run(e1, qa[kk], b2, b3);
+          } else {
+            Mma<T>::run(s0, qa[kk], b0, b1);
+            Mma<T>::run(s1, qa[kk], b2, b3);
+          }
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          s0[i] += e0[i];
+          s1[i] += e1[i];
+        }
+      }
+      auto ok = [&](int tok) { return tok < nvalid; };
+      const int ta = 2 * tq, tb = 2 * tq + 1, tc = 8 + 2 * tq, td = 9 + 2 * tq;
+      const float x0 = ok(ta) ? s0[0] * p.scale_log2 : -INFINITY;
+      const float x1 = ok(tb) ? s0[1] * p.scale_log2 : -INFINITY;
+      const float x2 = ok(tc) ? s1[0] * p.scale_log2 : -INFINITY;
+      const float x3 = ok(td) ? s1[1] * p.scale_log2 : -INFINITY;
+      float mx = fmaxf(fmaxf(x0, x1), fmaxf(x2, x3));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+      const float mn0 = fmaxf(m0, mx);
+      const float ms0 = mn0 == -INFINITY ? 0.f : mn0;
+      const float corr0 = exp2f(m0 - ms0);
+      const float p0 = exp2f(x0 - ms0), p1 = exp2f(x1 - ms0);
+      const float p2 = exp2f(x2 - ms0), p3 = exp2f(x3 - ms0);
+      l0 = l0 * corr0 + (p0 + p1 + p2 + p3);
+      m0 = mn0;
+      uint32_t pa[4];
+      pa[0] = Mma<T>::pack(p0, p1);
+      pa[2] = Mma<T>::pack(p2, p3);
+      pa[1] = pa[3] = 0u;
+      float corr1 = 1.f;
+      if constexpr (G16) {
+        const float y0 = ok(ta) ? s0[2] * p.scale_log2 : -INFINITY;
+        const float y1 = ok(tb) ? s0[3] * p.scale_log2 : -INFINITY;
+        const float y2 = ok(tc) ? s1[2] * p.scale_log2 : -INFINITY;
+        const float y3 = ok(td) ? s1[3] * p.scale_log2 : -INFINITY;
+        float my = fmaxf(fmaxf(y0, y1), fmaxf(y2, y3));
+        my = fmaxf(my, __shfl_xor_sync(0xffffffffu, my, 1));
+        my = fmaxf(my, __shfl_xor_sync(0xffffffffu, my, 2));
+        const float mn1 = fmaxf(m1, my);
+        const float ms1 = mn1 == -INFINITY ? 0.f : mn1;
+        corr1 = exp2f(m1 - ms1);
+        const float q0 = exp2f(y0 - ms1), q1 = exp2f(y1 - ms1);
+        const float q2 = exp2f(y2 - ms1), q3 = exp2f(y3 - ms1);
+        l1 = l1 * corr1 + (q0 + q1 + q2 + q3);
+        m1 = mn1;
+        pa[1] = Mma<T>::pack(q0, q1);
+        pa[3] = Mma<T>::pack(q2, q3);
+      }
+      if (__any_sync(0xffffffffu, corr0 != 1.f || corr1 != 1.f)) {  // a row max moved
+#pragma unroll
+        for (int n = 0; n < NT; ++n) {
+          o[n][0] *= corr0;
+          o[n][1] *= corr0;
+          if constexpr (G16) {
+            o[n][2] *= corr1;
+            o[n][3] *= corr1;
+          }
+        }
+      }
+      {
+        const int mi = lane >> 3;
+        const int rv = ((mi & 1) << 3) + (lane & 7);
+#pragma unroll
+        for (int np = 0; np < KS; ++np) {
+          const int c = ((np & 3) << 1) + (mi >> 1);
+          uint32_t b0, b1, b2, b3;
+          ldsm_x4_t(b0, b1, b2, b3, vbase + (np >> 2) * block_bytes + swz(rv, c));
+          Mma<T>::run(o[2 * np], pa, b0, b1);
+          Mma<T>::run(o[2 * np + 1], pa, b2, b3);
+        }
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);
+
+    if (!(flags & 2)) continue;
+    // ---- end of a run segment: combine the warps of this KV head ----------
+    const int buf = (p.scr_bufs == 2) ? (segments & 1) : 0;
+    ++segments;
+    const int RS = p.group * (D + 2);  // floats per warp in the scratch
+    float *mine = scratch + (static_cast<size_t>(buf) * kNC + warp) * RS;
+    {
+      float ls0 = l0 + __shfl_xor_sync(0xffffffffu, l0, 1);
+      ls0 += __shfl_xor_sync(0xffffffffu, ls0, 2);
+      float ls1 = l1 + __shfl_xor_sync(0xffffffffu, l1, 1);
+      ls1 += __shfl_xor_sync(0xffffffffu, ls1, 2);
+#pragma unroll
+      for (int n = 0; n < NT; ++n) {
+        if (gid < p.group)
+          *reinterpret_cast<float2 *>(mine + gid * (D + 2) + n * 8 + 2 * tq) =
+              make_float2(o[n][0], o[n][1]);
+        if (G16 && gid + 8 < p.group)
+          *reinterpret_cast<float2 *>(mine + (gid + 8) * (D + 2) + n * 8 + 2 * tq) =
+              make_float2(o[n][2], o[n][3]);
+      }
+      if (tq == 0) {
+        if (gid < p.group) {
+          mine[gid * (D + 2) + D] = m0;
+          mine[gid * (D + 2) + D + 1] = ls0;
+        }
+        if (G16 && gid + 8 < p.group) {
+          mine[(gid + 8) * (D + 2) + D] = m1;
+          mine[(gid + 8) * (D + 2) + D + 1] = ls1;
+        }
+      }
+    }
+    __syncwarp();
+    if (subs > 1) {
+      if (lane == 0) mbar_arrive(&hsync[h]);
+      if (!mbar_wait_bounded(&hsync[h], (segments - 1) & 1)) {
+        timed_out = true;
+        break;
+      }
+      if (sw != 0) continue;
+    }
+    // warp (h, 0): rows h*group .. h*group+group-1 of request rec.b
+    const int b = rec.b;
+    const bool direct = flags & 4;
+    constexpr int DPL = D / 32;
+    const float *first = scratch + (static_cast<size_t>(buf) * kNC + h * subs) * RS;
+    const int slot = cta + b;
+    for (int r = 0; r < p.group; ++r) {
+      float M = -INFINITY;
+      for (int j = 0; j < subs; ++j) M = fmaxf(M, first[j * RS + r * (D + 2) + D]);
+      float acc[DPL], L = 0.f;
+#pragma unroll
+      for (int i = 0; i < DPL; ++i) acc[i] = 0.f;
+      if (M != -INFINITY) {
+        for (int j = 0; j < subs; ++j) {
+          const float *row = first + j * RS + r * (D + 2);
+          const float w = exp2f(row[D] - M);
+          L += w * row[D + 1];
+#pragma unroll
+          for (int i = 0; i < DPL; ++i) acc[i] += w * row[i * 32 + lane];
+        }
+      }
+      const float inv = L > 0.f ? 1.f / L : 0.f;
+      const int qrow = h * p.group + r;
+      if (direct) {
+        T *ob = static_cast<T *>(p.out) + (static_cast<int64_t>(b) * p.hq + qrow) * D;
+#pragma unroll
+        for (int i = 0; i < DPL; ++i) ob[i * 32 + lane] = Elt<T>::from(acc[i] * inv);
+        if (p.lse && lane == 0)
+          p.lse[b * p.hq + qrow] = L > 0.f ? (M + __log2f(L)) * kLn2 : -INFINITY;
+      } else {
+        float *po = p.part_o + (static_cast<int64_t>(slot) * p.hq + qrow) * D;
+#pragma unroll
+        for (int i = 0; i < DPL; ++i) po[i * 32 + lane] = acc[i] * inv;
+        if (lane == 0) p.part_lse[slot * p.hq + qrow] = L > 0.f ? M + __log2f(L) : -INFINITY;
+      }
+    }
+  }
+  if (timed_out && lane == 0) flag(p.status, MI_STATUS_TIMEOUT);
+}
+
+// Split-K merge: one warp per (request, query head). Requests whose pages
+// all fall in one CTA's run were finished by the decode kernel; for the
+// others, combine the normalised partials of the runs that cover them
+// (slots first_run + b .. last_run + b), lanes over head_dim.
+template <typename T, int D>
+__global__ void __launch_bounds__(256) decode_sk_merge_kernel(const SkParams p, int grid_runs) {
+  constexpr int DPL = D / 32;
+  pdl_wait();  // every partial of the decode grid is written and visible
+  const int lane = threadIdx.x & 31;
+  const int wid = blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (wid >= p.batch * p.hq) return;
+  const int b = wid / p.hq, qrow = wid % p.hq;
+  const int base0 = p.indptr[0];
+  const int total = p.indptr[p.batch] - base0;
+  if (total <= 0) return;
+  const int run = cdiv(total, grid_runs);
+  const int start_b = p.indptr[b] - base0, end_b = p.indptr[b + 1] - base0;
+  if (end_b <= start_b) return;
+  const int first = start_b / run, nch = (end_b - 1) / run - first + 1;
+  if (nch <= 1) return;
+  const int slot0 = first + b;
+  // log-sum-exp of chunk c held by lane c % 32 (the first 32 stay in a register)
+  const float lse0 = lane < nch
+      ? __ldcg(p.part_lse + static_cast<int64_t>(slot0 + lane) * p.hq + qrow) : -INFINITY;
+  float M = lse0;
+  for (int c = lane + 32; c < nch; c += 32)
+    M = fmaxf(M, __ldcg(p.part_lse + static_cast<int64_t>(slot0 + c) * p.hq + qrow));
+  M = warp_max(M);
+  float acc[DPL], wsum = 0.f;
+#pragma unroll
+  for (int i = 0; i < DPL; ++i) acc[i] = 0.f;
+  if (M != -INFINITY) {
+    for (int c0 = 0; c0 < nch; c0 += 32) {
+      const int c = c0 + lane;
+      const float lc = c0 == 0 ? lse0
+          : (c < nch ? __ldcg(p.part_lse + static_cast<int64_t>(slot0 + c) * p.hq + qrow)
+                     : -INFINITY);
+      const float w = c < nch ? exp2f(lc - M) : 0.f;
+      wsum += w;
+      const int cn = min(32, nch - c0);
+#pragma unroll 4
+      for (int j = 0; j < cn; ++j) {
+        const float wj = __shfl_sync(0xffffffffu, w, j);
+        const float *src = p.part_o + (static_cast<int64_t>(slot0 + c0 + j) * p.hq + qrow) * D;
+#pragma unroll
+        for (int i = 0; i < DPL; ++i) acc[i] += wj * __ldcg(src + i * 32 + lane);
+      }
+    }
+  }
+  wsum = warp_sum(wsum);
+  const float inv = wsum > 0.f ? 1.f / wsum : 0.f;
+  T *ob = static_cast<T *>(p.out) + (static_cast<int64_t>(b) * p.hq + qrow) * D;
+#pragma unroll
+  for (int i = 0; i < DPL; ++i) ob[i * 32 + lane] = Elt<T>::from(acc[i] * inv);
+  if (p.lse && lane == 0)
+    p.lse[b * p.hq + qrow] = wsum > 0.f ? (M + __log2f(wsum)) * kLn2 : -INFINITY;
+}
+
+// ---------------------------------------------------------------------------
+// host side: tensor maps (cached per pool), launch
+// ---------------------------------------------------------------------------
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void *ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &ptr, 12000,
+                                         cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  });
+  return fn;
+}
+
+struct MapEntry {
+  const void *base;
+  int64_t pages;
+  int ps, hkv, d, dtype;
+  CUtensorMap map;
+};
+
+std::mutex g_map_mu;
+MapEntry g_maps[512];
+int g_map_count = 0, g_map_next = 0;
+
+// Tensor map over one layer's pool: dims (d, head, slot, page*2+kv), natural
+// NHD strides; box = 64 d x 1 head x 16 slots x 1, 128-byte swizzle.
+bool pool_map(const SkArgs &a, CUtensorMap *out) {
+  std::lock_guard<std::mutex> lock(g_map_mu);
+  for (int i = 0; i < g_map_count; ++i) {
+    const MapEntry &e = g_maps[i];
+    if (e.base == a.kv && e.pages == a.num_pages && e.ps == a.ps && e.hkv == a.hkv &&
+        e.d == a.d && e.dtype == a.dtype) {
+      *out = e.map;
+      return true;
+    }
+  }
+  auto fn = encode_fn();
+  if (!fn) return false;
+  const cuuint64_t es = 2;
+  cuuint64_t dims[4] = {static_cast<cuuint64_t>(a.d), static_cast<cuuint64_t>(a.hkv),
+                        static_cast<cuuint64_t>(a.ps),
+                        static_cast<cuuint64_t>(a.num_pages) * 2};
+  cuuint64_t strides[3] = {static_cast<cuuint64_t>(a.d) * es,
+                           static_cast<cuuint64_t>(a.hkv) * a.d * es,
+                           static_cast<cuuint64_t>(a.ps) * a.hkv * a.d * es};
+  cuuint32_t box[4] = {64, 1, static_cast<cuuint32_t>(kTile), 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  MapEntry e{a.kv, a.num_pages, a.ps, a.hkv, a.d, a.dtype, {}};
+  CUresult r = fn(&e.map,
+                  a.dtype == MI_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                           : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                  4, const_cast<void *>(a.kv), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return false;
+  if (g_map_count < 512) {
+    g_maps[g_map_count++] = e;
+  } else {
+    g_maps[g_map_next] = e;
+    g_map_next = (g_map_next + 1) % 512;
+  }
+  *out = e.map;
+  return true;
+}
+
+struct SkLayout {
+  int stages, stage_bytes, bar_off, rec_off, scr_off, scr_bufs, meta_off, smem;
+};
+
+bool sk_layout(int hkv, int d, int group, int batch, SkLayout *L) {
+  const int subs = kNC / hkv;
+  L->stage_bytes = 2 * hkv * kTile * d * 2;
+  L->scr_bufs = subs > 1 ? 2 : 1;
+  const int scr = L->scr_bufs * kNC * group * (d + 2) * 4;
+  const int meta = batch <= kSmemBatch ? (2 * kSmemBatch + 4) * 4 : 0;
+  const int fixed =
+      1024 /*align slack*/ + (2 * kMaxStages + 8) * 8 + kMaxStages * 16 + scr + meta;
+  int s = (kSmemLimit - fixed) / L->stage_bytes;
+  if (s > kMaxStages) s = kMaxStages;
+  if (s < 2) return false;
+  L->stages = s;
+  L->bar_off = s * L->stage_bytes;
+  L->rec_off = L->bar_off + (2 * kMaxStages + 8) * 8;
+  L->scr_off = L->rec_off + kMaxStages * 16;
+  L->meta_off = meta ? L->scr_off + scr : -1;
+  L->smem = L->scr_off + scr + meta + 1024;
+  return L->smem <= kSmemLimit;
+}
+
+template <typename T, int D, bool G16>
+int launch_sk_t(const SkArgs &a, const CUtensorMap &map, const SkParams &p, int grid,
+                int smem) {
+  static unsigned long long attr_set = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!(attr_set >> (dev & 63) & 1ull)) {
+    if (cudaFuncSetAttribute(decode_sk_kernel<T, D, G16>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             kSmemLimit) != cudaSuccess)
+      return check_launch("decode_sk_kernel smem attribute");
+    attr_set |= 1ull << (dev & 63);
+  }
+  cudaError_t e = launch_pdl(decode_sk_kernel<T, D, G16>, dim3(grid), dim3(kThreads), smem,
+                             a.stream, map, p);
+  if (e != cudaSuccess) return fail(MI_ERR_CUDA, "decode_sk_kernel launch: %s", cudaGetErrorString(e));
+  const int warps = a.batch * a.hq;
+  e = launch_pdl(decode_sk_merge_kernel<T, D>, dim3((warps + 7) / 8), dim3(256), 0, a.stream, p,
+                 grid);
+  if (e != cudaSuccess)
+    return fail(MI_ERR_CUDA, "decode_sk_merge_kernel launch: %s", cudaGetErrorString(e));
+  return check_launch("decode_sk_merge_kernel");
+}
+
+}  // namespace
+
+size_t decode_sk_workspace_bytes(int batch, int hq, int hkv, int d) {
+  const size_t slots = static_cast<size_t>(num_sms()) + batch;
+  return kCtrl + al256(size_t(batch) * hkv * 4) + al256(slots * hq * d * 4) +
+         al256(slots * hq * 4);
+}
+
+// Returns -1 when the shape/arguments are outside this kernel's coverage.
+int launch_decode_sk(const SkArgs &a) {
+  if (!(a.dtype == MI_DTYPE_BF16 || a.dtype == MI_DTYPE_F16)) return -1;
+  if (!(a.d == 64 || a.d == 128)) return -1;
+  if (!(a.hkv == 1 || a.hkv == 2 || a.hkv == 4 || a.hkv == 8)) return -1;
+  if (a.ps % kTile != 0 || a.ps > 256) return -1;
+  const int group = a.hq / a.hkv;
+  if (group > 16 || a.qsb % 2 || a.qsh % 2) return -1;
+  if ((reinterpret_cast<uintptr_t>(a.kv) & 15) || (reinterpret_cast<uintptr_t>(a.q) & 3) ||
+      (reinterpret_cast<uintptr_t>(a.ws) & 255))
+    return -1;
+  if (a.num_pages * 2 > (1LL << 31)) return -1;
+  if (a.ws == nullptr || a.ws_bytes < decode_sk_workspace_bytes(a.batch, a.hq, a.hkv, a.d))
+    return -1;
+  SkLayout L;
+  if (!sk_layout(a.hkv, a.d, group, a.batch, &L)) return -1;
+  CUtensorMap map;
+  if (!pool_map(a, &map)) return -1;
+  const int grid = num_sms();
+  unsigned char *w = static_cast<unsigned char *>(a.ws);
+  const size_t slots = static_cast<size_t>(grid) + a.batch;
+  SkParams p{};
+  p.q = a.q;
+  p.qsb = a.qsb;
+  p.qsh = a.qsh;
+  p.num_pages = a.num_pages;
+  p.ps = a.ps;
+  p.hkv = a.hkv;
+  p.group = group;
+  p.hq = a.hq;
+  p.batch = a.batch;
+  p.subs = kNC / a.hkv;
+  p.stages = L.stages;
+  p.stage_bytes = L.stage_bytes;
+  p.indptr = a.indptr;
+  p.indices = a.indices;
+  p.last = a.last;
+  p.scale_log2 = a.sm_scale * kLog2e;
+  p.out = a.out;
+  p.lse = a.lse;
+  p.status = a.status;
+  p.arrive = reinterpret_cast<unsigned *>(w + kCtrl);
+  p.part_o = reinterpret_cast<float *>(w + kCtrl + al256(size_t(a.batch) * a.hkv * 4));
+  p.part_lse = reinterpret_cast<float *>(reinterpret_cast<unsigned char *>(p.part_o) +
+                                         al256(slots * a.hq * a.d * 4));
+  p.bar_off = L.bar_off;
+  p.rec_off = L.rec_off;
+  p.scr_off = L.scr_off;
+  p.scr_bufs = L.scr_bufs;
+  p.meta_off = L.meta_off;
+  const bool g16 = group > 8;
+  if (a.dtype == MI_DTYPE_BF16) {
+    if (a.d == 128)
+      return g16 ? launch_sk_t<__nv_bfloat16, 128, true>(a, map, p, grid, L.smem)
+                 : launch_sk_t<__nv_bfloat16, 128, false>(a, map, p, grid, L.smem);
+    return g16 ? launch_sk_t<__nv_bfloat16, 64, true>(a, map, p, grid, L.smem)
+               : launch_sk_t<__nv_bfloat16, 64, false>(a, map, p, grid, L.smem);
+  }
+  if (a.d == 128)
+    return g16 ? launch_sk_t<__half, 128, true>(a, map, p, grid, L.smem)
+               : launch_sk_t<__half, 128, false>(a, map, p, grid, L.smem);
+  return g16 ? launch_sk_t<__half, 64, true>(a, map, p, grid, L.smem)
+             : launch_sk_t<__half, 64, false>(a, map, p, grid, L.smem);
+}
+
+}  // namespace mi

@@ -225,7 +225,7 @@ def check_decode(c, ws=None):
 
 @pytest.mark.parametrize("dtype", ["bfloat16", "float16", "float32"])
 @pytest.mark.parametrize("hq,hkv,d", [(32, 8, 128), (28, 4, 128), (14, 2, 64), (64, 8, 128),
-                                      (8, 8, 128), (16, 1, 64)])
+                                      (8, 8, 128), (16, 1, 64), (32, 16, 128), (8, 1, 128)])
 def test_decode_ragged_edges(dtype, hq, hkv, d):
     lens = [0, 1, 15, 16, 17, 31, 32, 33, 250, 1023]
     check_decode(paged_case(11, lens, hq, hkv, d, dtype=dtype))
@@ -253,6 +253,7 @@ def test_decode_workspace_reuse_and_page_size_8():
     for seed in range(3):
         check_decode(paged_case(20 + seed, [700, 5, 1400], 32, 8, 128), ws)
     check_decode(paged_case(30, [37, 64, 129], 14, 2, 64, page_size=8))
+    check_decode(paged_case(31, [37, 64, 129, 1000], 32, 8, 128, page_size=32))
 
 
 def test_decode_bad_page_is_flagged():
