@@ -74,14 +74,22 @@ struct __align__(16) StageRec {
   int b, tok0, kvlen, flags;  // flags: 1 first, 2 last, 4 direct, 8 bad page; ordinal << 8
 };
 
+// 4-D TMA tile load with an L2 cache policy (the KV stream is read once:
+// evict-first keeps it from pushing partials and metadata out of L2).
 __device__ __forceinline__ void tma_load_4d(void *dst, const CUtensorMap *map, int c0, int c1,
-                                            int c2, int c3, uint64_t *bar) {
+                                            int c2, int c3, uint64_t *bar, uint64_t policy) {
   asm volatile(
       "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(smem_u32(dst)),
+      ".L2::cache_hint [%0], [%1, {%2, %3, %4, %5}], [%6], %7;" ::"r"(smem_u32(dst)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3),
-      "r"(smem_u32(bar))
+      "r"(smem_u32(bar)), "l"(policy)
       : "memory");
+}
+
+__device__ __forceinline__ uint64_t evict_first_policy() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
 }
 
 __device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
@@ -152,6 +160,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == kNC) {
     int k = 0;
     bool ok_run = true;
+    const uint64_t policy = evict_first_policy();
     const int lo = cta * run, hi = min(total, lo + run);
     if (lo < hi) {
       int b = 0;
@@ -207,7 +216,8 @@ __global__ void __launch_bounds__(kThreads, 1)
               const int dh = rest % DH, which = rest / DH;
               unsigned char *dst = smem + s * p.stage_bytes + (which * DH + dh) * block_bytes +
                                    h * (kTile * 128);
-              tma_load_4d(dst, &tmap, dh * 64, h, tok0 % p.ps, page * 2 + which, &full[s]);
+              tma_load_4d(dst, &tmap, dh * 64, h, tok0 % p.ps, page * 2 + which, &full[s],
+                          policy);
             }
           }
           ++k;
