@@ -175,6 +175,62 @@ def cpu_reference_steps(lens, steps, budget_s=20.0):
 
 
 # ---------------------------------------------------------------------------
+# Mistral-7B-shape continuous-batching decode @ B=32
+# ---------------------------------------------------------------------------
+def model_decode(dev, batch=32, out_tokens=50, seed=3):
+    """Decode tok/s of the Mistral-7B shape (random bf16 weights) at batch 32.
+
+    32 requests with prompts U[128, 1024] of random ids, 50 output tokens
+    each (1 from prefill + 49 decode steps), page_size 16, CUDA-graph decode
+    through this package's Scheduler. T2T follows the reference's definition
+    (scheduler.py:984-995, benchmark.py:57-62): per request, the time between
+    its first and last token divided by (tokens - 1); tok/s = batch / T2T.
+    """
+    import torch
+    from mi_b200.model import PRESETS, Model
+    from mi_b200.scheduler import Request, Scheduler
+    from mi_b200.weights import init_random_weights
+    cfg = PRESETS["mistral-7b"]
+    model = Model(cfg).to(device=dev, dtype=torch.bfloat16)
+    init_random_weights(model, seed, generator_device="cuda")
+    model.eval().prepare()
+    rng = np.random.default_rng(seed)
+    lens = rng.integers(128, 1025, batch).tolist()
+    prompts = [rng.integers(0, cfg.vocab_size, n).tolist() for n in lens]
+    sched = Scheduler(model, cfg, dev, torch.bfloat16, max_batch_size=batch,
+                      max_seq_len=1024 + out_tokens + 16, page_size=16, eos_token_ids=set())
+    # warm-up request set (fills caches / allocator paths), then the measured one
+    for rep in range(2):
+        reqs = [Request(f"w{rep}_{i}", p, out_tokens if rep else 4, 0.0)
+                for i, p in enumerate(prompts)]
+        for r in reqs:
+            sched.submit_request(r)
+        torch.cuda.synchronize()
+        step_ms = []
+        t_start = time.perf_counter()
+        while sched.active_requests or sched.waiting_queue:
+            t0 = time.perf_counter()
+            sched.step()
+            step_ms.append((time.perf_counter() - t0) * 1e3)
+        total_s = time.perf_counter() - t_start
+    t2t = [(r.last_token_time - r.prefill_done_time) / (len(r.generated_tokens) - 1)
+           for r in reqs]
+    t2t_ms = statistics.mean(t2t) * 1e3
+    decode_steps = step_ms[1:]  # the first step holds the prefill
+    out = {"metric": "Mistral-7B-shape decode tok/s @B=32 (config 3)",
+           "value": round(batch / (t2t_ms / 1e3), 1), "unit": "tok/s",
+           "t2t_ms": round(t2t_ms, 3),
+           "decode_step_ms_median": round(statistics.median(decode_steps), 3),
+           "first_step_ms (prefill of all 32 + 1 decode)": round(step_ms[0], 2),
+           "wall_s": round(total_s, 3), "batch": batch, "output_tokens": out_tokens,
+           "prompt_lens": "U[128,1024] seeded", "weights": "random N(0,0.02) bf16",
+           "cuda_graph_decode": True}
+    del sched, model
+    torch.cuda.empty_cache()
+    return out
+
+
+# ---------------------------------------------------------------------------
 def parse_args():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -185,6 +241,8 @@ def parse_args():
                     help="layer pools per step (32 = Mistral-7B; fewer only for profiling)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-model", action="store_true",
+                    help="skip the Mistral-7B-shape decode measurement (config 3)")
     return ap.parse_args()
 
 
@@ -407,6 +465,13 @@ def main():
         cpu = {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
                "sample": sample}
 
+    # ---- config 3: model decode tok/s (rank 0, N = 1) --------------------------
+    model_line = None
+    if rank == 0 and world == 1 and not args.no_model:
+        del pools
+        torch.cuda.empty_cache()
+        model_line = model_decode(dev)
+
     if world > 1:
         dist.destroy_process_group()
     if rank != 0:
@@ -422,7 +487,8 @@ def main():
                      "traffic": traffic, "algorithmic_bytes": decode_bytes(lens),
                      "avg_launch_us": round(dec_ms * 1e3, 2)},
         "cpu_baseline": cpu, "e2e": e2e, "clocks": clk,
-        "gpu_launches": 2 * K * L,
+        "gpu_launches": 3 * K * L,
+        "model_decode": model_line,
     }
     print(json.dumps(line), flush=True)
 
