@@ -268,7 +268,7 @@ __global__ void __launch_bounds__(TcCfg<D>::NW * 32, 1) decode_tc_kernel(const D
   while (consumed < issued) {
     const int s = consumed % S;
     const uint32_t phase = (consumed / S) & 1;
-    if (!mbar_wait_bounded(&my_bars[s], phase)) {
+    if (!__all_sync(0xffffffffu, mbar_wait_bounded(&my_bars[s], phase))) {
       timed_out = true;
       break;
     }

@@ -38,6 +38,7 @@
 #include "mi_common.cuh"
 
 #include "decode_sk.cuh"
+#include "tma.cuh"
 
 namespace mi {
 namespace {
@@ -73,33 +74,6 @@ constexpr int kSmemBatch = 1024;  // requests whose metadata fits the shared-mem
 struct __align__(16) StageRec {
   int b, tok0, kvlen, flags;  // flags: 1 first, 2 last, 4 direct, 8 bad page; ordinal << 8
 };
-
-// 4-D TMA tile load with an L2 cache policy (the KV stream is read once:
-// evict-first keeps it from pushing partials and metadata out of L2).
-__device__ __forceinline__ void tma_load_4d(void *dst, const CUtensorMap *map, int c0, int c1,
-                                            int c2, int c3, uint64_t *bar, uint64_t policy) {
-  asm volatile(
-      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
-      ".L2::cache_hint [%0], [%1, {%2, %3, %4, %5}], [%6], %7;" ::"r"(smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3),
-      "r"(smem_u32(bar)), "l"(policy)
-      : "memory");
-}
-
-__device__ __forceinline__ uint64_t evict_first_policy() {
-  uint64_t pol;
-  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
-  return pol;
-}
-
-__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
-
-// Offset of 16-byte chunk `c` of row `r` in a 128-byte-swizzled box.
-__device__ __forceinline__ uint32_t swz(int r, int c) {
-  return static_cast<uint32_t>(r * 128 + ((c ^ (r & 7)) << 4));
-}
 
 template <typename T, int D, bool G16>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -196,7 +170,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int page = __shfl_sync(0xffffffffu, pw, gpos - wbase);
           const bool bad = page < 0 || page >= p.num_pages;
           const int s = k % S;
-          if (!mbar_wait_bounded(&empty[s], ((k / S) & 1) ^ 1)) {
+          if (!__all_sync(0xffffffffu, mbar_wait_bounded(&empty[s], ((k / S) & 1) ^ 1))) {
             ok_run = false;
             break;
           }
@@ -229,7 +203,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool sentinel = false;
     if (ok_run) {
       const int s = k % S;
-      if (mbar_wait_bounded(&empty[s], ((k / S) & 1) ^ 1)) {
+      if (__all_sync(0xffffffffu, mbar_wait_bounded(&empty[s], ((k / S) & 1) ^ 1))) {
         if (lane == 0) {
           recs[s] = StageRec{-1, 0, 0, 0};
           mbar_arrive(&full[s]);
@@ -270,7 +244,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   for (int k = 0;; ++k) {
     const int s = k % S;
-    if (!mbar_wait_bounded(&full[s], (k / S) & 1)) {
+    if (!__all_sync(0xffffffffu, mbar_wait_bounded(&full[s], (k / S) & 1))) {
       timed_out = true;
       break;
     }
@@ -448,7 +422,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
     if (subs > 1) {
       if (lane == 0) mbar_arrive(&hsync[h]);
-      if (!mbar_wait_bounded(&hsync[h], (segments - 1) & 1)) {
+      if (!__all_sync(0xffffffffu, mbar_wait_bounded(&hsync[h], (segments - 1) & 1))) {
         timed_out = true;
         break;
       }
@@ -555,72 +529,6 @@ __global__ void __launch_bounds__(256) decode_sk_merge_kernel(const SkParams p, 
 // ---------------------------------------------------------------------------
 // host side: tensor maps (cached per pool), launch
 // ---------------------------------------------------------------------------
-PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void *ptr = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &ptr, 12000,
-                                         cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
-  });
-  return fn;
-}
-
-struct MapEntry {
-  const void *base;
-  int64_t pages;
-  int ps, hkv, d, dtype;
-  CUtensorMap map;
-};
-
-std::mutex g_map_mu;
-MapEntry g_maps[512];
-int g_map_count = 0, g_map_next = 0;
-
-// Tensor map over one layer's pool: dims (d, head, slot, page*2+kv), natural
-// NHD strides; box = 64 d x 1 head x 16 slots x 1, 128-byte swizzle.
-bool pool_map(const SkArgs &a, CUtensorMap *out) {
-  std::lock_guard<std::mutex> lock(g_map_mu);
-  for (int i = 0; i < g_map_count; ++i) {
-    const MapEntry &e = g_maps[i];
-    if (e.base == a.kv && e.pages == a.num_pages && e.ps == a.ps && e.hkv == a.hkv &&
-        e.d == a.d && e.dtype == a.dtype) {
-      *out = e.map;
-      return true;
-    }
-  }
-  auto fn = encode_fn();
-  if (!fn) return false;
-  const cuuint64_t es = 2;
-  cuuint64_t dims[4] = {static_cast<cuuint64_t>(a.d), static_cast<cuuint64_t>(a.hkv),
-                        static_cast<cuuint64_t>(a.ps),
-                        static_cast<cuuint64_t>(a.num_pages) * 2};
-  cuuint64_t strides[3] = {static_cast<cuuint64_t>(a.d) * es,
-                           static_cast<cuuint64_t>(a.hkv) * a.d * es,
-                           static_cast<cuuint64_t>(a.ps) * a.hkv * a.d * es};
-  cuuint32_t box[4] = {64, 1, static_cast<cuuint32_t>(kTile), 1};
-  cuuint32_t estr[4] = {1, 1, 1, 1};
-  MapEntry e{a.kv, a.num_pages, a.ps, a.hkv, a.d, a.dtype, {}};
-  CUresult r = fn(&e.map,
-                  a.dtype == MI_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
-                                           : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
-                  4, const_cast<void *>(a.kv), dims, strides, box, estr,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) return false;
-  if (g_map_count < 512) {
-    g_maps[g_map_count++] = e;
-  } else {
-    g_maps[g_map_next] = e;
-    g_map_next = (g_map_next + 1) % 512;
-  }
-  *out = e.map;
-  return true;
-}
-
 struct SkLayout {
   int stages, stage_bytes, bar_off, rec_off, scr_off, scr_bufs, meta_off, smem;
 };
@@ -694,7 +602,7 @@ int launch_decode_sk(const SkArgs &a) {
   SkLayout L;
   if (!sk_layout(a.hkv, a.d, group, a.batch, &L)) return -1;
   CUtensorMap map;
-  if (!pool_map(a, &map)) return -1;
+  if (!pool_tensor_map(a.kv, a.num_pages, a.ps, a.hkv, a.d, a.dtype, &map)) return -1;
   const int grid = num_sms();
   unsigned char *w = static_cast<unsigned char *>(a.ws);
   const size_t slots = static_cast<size_t>(grid) + a.batch;

@@ -11,28 +11,9 @@
 // included) and any head_dim <= 256. The tensor-core path lives in
 // prefill_tc.cu.
 #include "mi_common.cuh"
+#include "prefill.cuh"
 
 namespace mi {
-
-struct PrefillParams {
-  const void *q;
-  int64_t qsn, qsh;
-  const int32_t *qo_indptr;
-  int total_q;
-  const void *kv;
-  int64_t num_pages;
-  int ps, hkv, d;
-  const int32_t *indptr, *indices, *last;
-  int batch, hq, group, causal;
-  float scale_log2;
-  void *out;
-  float *lse;
-  int32_t *status;
-};
-
-// defined in prefill_tc.cu: returns -1 when the shape is not covered there
-int launch_prefill_tc(const PrefillParams &p, int dtype, cudaStream_t s);
-
 namespace {
 
 constexpr int kRowsPerCta = 4;

@@ -1,0 +1,30 @@
+// Arguments shared by the generic (prefill.cu) and tensor-core
+// (prefill_tc.cu) paged prefill kernels.
+#pragma once
+
+#include "mi_common.cuh"
+
+namespace mi {
+
+struct PrefillParams {
+  const void *q;
+  int64_t qsn, qsh;
+  const int32_t *qo_indptr;
+  int total_q;
+  const void *kv;
+  int64_t num_pages;
+  int ps, hkv, d;
+  const int32_t *indptr, *indices, *last;
+  int batch, hq, group, causal;
+  float scale_log2;
+  void *out;
+  float *lse;
+  int32_t *status;
+};
+
+// Tensor-core path (prefill_tc.cu). Returns -1 (nothing launched) when the
+// shape or layout is outside its coverage, so the caller runs the generic
+// kernel instead.
+int launch_prefill_tc(const PrefillParams &p, int dtype, cudaStream_t s);
+
+}  // namespace mi

@@ -1,0 +1,65 @@
+// TMA tensor maps over the page pool and queries, and the device-side TMA /
+// mbarrier helpers shared by the decode and prefill kernels.
+#pragma once
+
+#include <cuda.h>
+
+#include "mi_common.cuh"
+
+namespace mi {
+
+// Tensor map over one layer's pool kv_data[P][2][ps][Hkv][D] (bf16/fp16):
+// dims (d, head, slot, page*2 + kv) with the natural NHD strides, box =
+// 64 d x 1 head x 16 slots x 1, 128-byte swizzle. Cached per pool.
+bool pool_tensor_map(const void *kv, int64_t num_pages, int ps, int hkv, int d, int dtype,
+                     CUtensorMap *out);
+// Tensor map over rows[n][h][d] (element strides sn, sh; d contiguous):
+// dims (d, h, n), box = 64 d x box_h x box_n, 128-byte swizzle. Not cached.
+bool rows_tensor_map(const void *base, int64_t n, int h, int d, int64_t sn, int64_t sh,
+                     int box_h, int box_n, int dtype, CUtensorMap *out);
+
+// 3-/4-D TMA tile loads completing on an mbarrier, with an L2 cache policy.
+__device__ __forceinline__ void tma_load_4d(void *dst, const CUtensorMap *map, int c0, int c1,
+                                            int c2, int c3, uint64_t *bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      ".L2::cache_hint [%0], [%1, {%2, %3, %4, %5}], [%6], %7;" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3),
+      "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, int c0, int c1,
+                                            int c2, uint64_t *bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      ".L2::cache_hint [%0], [%1, {%2, %3, %4}], [%5], %6;" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar)),
+      "l"(policy)
+      : "memory");
+}
+
+// The KV stream is read once: evict-first keeps it from pushing partials and
+// metadata out of L2. Queries are reused by every KV tile: evict-last.
+__device__ __forceinline__ uint64_t evict_first_policy() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+__device__ __forceinline__ uint64_t evict_last_policy() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// Offset of 16-byte chunk `c` of row `r` in a 128-byte-swizzled box whose
+// base is 1024-byte aligned (the hardware XORs the chunk with row % 8).
+__device__ __forceinline__ uint32_t swz(int r, int c) {
+  return static_cast<uint32_t>(r * 128 + ((c ^ (r & 7)) << 4));
+}
+
+}  // namespace mi
