@@ -249,6 +249,23 @@ int mi_step_prepare(int32_t *free_ring, int32_t *pool_ctrl, int32_t num_pages,
                     int32_t *kv_last_page_len, int32_t *append_positions,
                     int32_t *status, mi_stream_t stream);
 
+/* ---- decode-step glue (model.py:115-122, :301-311, :333-343) ---------- */
+
+/* residual[r] = residual[r] + x[r] (rounded to dtype; skipped when x is
+ * NULL), then out[r] = rms_norm(residual[r]) * weight with fp32 statistics:
+ * the reference's `h = h + sublayer(...)` followed by F.rms_norm
+ * (model.py:115-122, :333-343) in one launch. Rows are contiguous
+ * [rows, hidden]; residual is updated in place; out must not alias it. */
+int mi_add_rmsnorm(const void *x, void *residual, const void *weight, void *out,
+                   int32_t rows, int32_t hidden, float eps, int32_t dtype,
+                   mi_stream_t stream);
+
+/* out[r, :] = silu(gate_up[r, :inter]) * gate_up[r, inter:] for contiguous
+ * [rows, 2*inter] input (the fused gate/up GEMM output): the reference's
+ * `F.silu(gate_proj(x)) * up_proj(x)` (model.py:311). */
+int mi_silu_mul(const void *gate_up, void *out, int32_t rows, int32_t inter, int32_t dtype,
+                mi_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

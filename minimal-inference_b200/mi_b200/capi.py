@@ -70,6 +70,8 @@ _SIGS = {
     "mi_step_prepare": ([_c_p, _c_p, _c_i32, _c_p, _c_p, _c_i32, _c_i32, _c_p, _c_p, _c_i32,
                          _c_i32, _c_i32, _c_p, _c_p, _c_i32, _c_p, _c_p, _c_p, _c_p],
                         ctypes.c_int),
+    "mi_add_rmsnorm": ([_c_p, _c_p, _c_p, _c_p, _c_i32, _c_i32, _c_f, _c_i32, _c_p], ctypes.c_int),
+    "mi_silu_mul": ([_c_p, _c_p, _c_i32, _c_i32, _c_i32, _c_p], ctypes.c_int),
 }
 
 _lib = None

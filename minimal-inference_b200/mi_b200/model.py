@@ -13,8 +13,11 @@ The attention step goes through the library kernels: one fused append launch
 applies RoPE to Q and K (the reference's ``apply_rotary_emb`` rounding,
 bit-identical) and scatters K/V into the layer's pages; then paged decode or
 paged prefill attention with native GQA (no head padding). There is no padded
-CPU path: ``attn_backend`` is required. GEMMs, RMSNorm and SiLU stay in torch
-(cuBLAS); Q/K/V and gate/up run as one GEMM each over fused weight views.
+CPU path: ``attn_backend`` is required. GEMMs stay in torch (cuBLAS); Q/K/V and
+gate/up run as one GEMM each over fused weight views. Each residual add runs
+fused with the RMSNorm that follows it, and SiLU(gate) * up is one kernel
+(``glue``), so a decoder layer is five GEMMs, two attention-path launches and
+three glue launches.
 """
 from __future__ import annotations
 
@@ -26,6 +29,7 @@ import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
+from .glue import add_rmsnorm, silu_mul
 from .page import append_paged_kv_cache
 from .rope import rope_tables
 
@@ -176,9 +180,7 @@ class MLP(nn.Module):
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         if self._gu_w is None:
             self.fuse()
-        gu = F.linear(x, self._gu_w)
-        g, u = gu.chunk(2, dim=-1)
-        return self.down_proj(F.silu(g) * u)
+        return self.down_proj(silu_mul(F.linear(x, self._gu_w)))
 
 
 class DecoderLayer(nn.Module):
@@ -190,9 +192,22 @@ class DecoderLayer(nn.Module):
         self.mlp = MLP(config, shard.get("intermediate_size"))
 
     def forward(self, x, cos, sin, mask, kv_cache=None, position_ids=None, attn_backend=None):
-        x = x + self.self_attn(self.input_layernorm(x), cos, sin, mask, kv_cache,
-                               position_ids, attn_backend)
-        return x + self.mlp(self.post_attention_layernorm(x))
+        """Reference signature (model.py:322-343); returns the new residual."""
+        h = x.contiguous().clone()
+        h.add_(self.residual_step(h, None, position_ids, attn_backend))
+        return h
+
+    def residual_step(self, h, pending, position_ids, attn_backend):
+        """One layer on the residual stream ``h`` (updated in place).
+
+        ``pending`` is the previous layer's MLP output not yet added to ``h``
+        (None for the first layer); the add runs fused into this layer's input
+        RMSNorm. Returns this layer's MLP output, likewise not yet added."""
+        y = add_rmsnorm(pending, h, self.input_layernorm.weight, self.input_layernorm.eps)
+        a = self.self_attn(y, None, None, None, None, position_ids, attn_backend)
+        y = add_rmsnorm(a, h, self.post_attention_layernorm.weight,
+                        self.post_attention_layernorm.eps)
+        return self.mlp(y)
 
 
 class Model(nn.Module):
@@ -223,14 +238,17 @@ class Model(nn.Module):
         flat token indices whose logits are wanted; returns ``[1, len, V]``."""
         if attn_backend is None:
             raise RuntimeError("mi_b200 has no padded/CPU attention path: pass attn_backend")
-        h = self.embed_tokens(input_ids)
+        h = self.embed_tokens(input_ids)          # residual stream, updated in place
         attn_backend.rope_cos = self.cos_cached
         attn_backend.rope_sin = self.sin_cached
+        pending = None
         for layer in self.layers:
-            h = layer(h, None, None, None, None, position_ids, attn_backend)
+            pending = layer.residual_step(h, pending, position_ids, attn_backend)
+        # last residual add + final norm; the norm is per row, so selecting
+        # rows after it equals selecting before
+        h = add_rmsnorm(pending, h, self.norm.weight, self.norm.eps)
         if logits_rows is not None:
             h = h.reshape(-1, h.shape[-1])[logits_rows].unsqueeze(0)
-        h = self.norm(h)
         if self.lm_head is not None:
             return self.lm_head(h)
         return F.linear(h, self.embed_tokens.weight)
