@@ -98,7 +98,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   if (threadIdx.x >= 32 && threadIdx.x < 32 + p.hkv) mbar_init(&hsync[threadIdx.x - 32], p.subs);
   pdl_trigger();  // the merge kernel may get scheduled next to this grid
-  pdl_wait();     // the append that wrote this step's K/V and q has finished
+  // Launched with PDL, this grid may start while the kernel before it (the
+  // append that writes this step's K/V and q) still runs. Everything up to
+  // the pdl_wait() calls below reads only the page-table metadata
+  // (kv_indptr / kv_indices / kv_last_page_len), which no kernel of this
+  // library that triggers its dependents early writes; the K/V tiles, q,
+  // the outputs and the workspace are touched only after pdl_wait().
   // The producer's first page-id window only needs this CTA's run start, so
   // its loads go out together with the metadata staging below.
   int pre_pw = -1, pre_pwn = -1;
@@ -148,6 +153,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       int wbase = lo;
       int pw = pre_pw, pwn = pre_pwn;  // loaded during the prologue
+      pdl_wait();  // the predecessor's K/V writes are visible to the TMA loads
       for (int pos = lo; pos < hi && ok_run;) {
         while (ip[b + 1] - base0 <= pos) ++b;
         const int start_b = ip[b] - base0, end_b = ip[b + 1] - base0;
@@ -223,6 +229,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 
   // =========================== consumer warps =============================
+  pdl_wait();  // q, out, lse and the workspace are the predecessor's to finish with
   const int subs = p.subs;
   const int h = warp / subs, sw = warp % subs;
   const int gid = lane >> 2, tq = lane & 3;
@@ -468,56 +475,71 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (timed_out && lane == 0) flag(p.status, MI_STATUS_TIMEOUT);
 }
 
-// Split-K merge: one warp per (request, query head). Requests whose pages
+// Split-K merge: one warp per (request, query head), two per CTA (small
+// CTAs find room next to the decode CTAs sooner). Requests whose pages
 // all fall in one CTA's run were finished by the decode kernel; for the
 // others, combine the normalised partials of the runs that cover them
-// (slots first_run + b .. last_run + b), lanes over head_dim.
+// (slots first_run + b .. last_run + b), lanes over head_dim. The run range
+// comes from kv_indptr before the wait (metadata only); after it, the lse
+// and the partial rows of up to kBatch runs are loaded in one round.
 template <typename T, int D>
-__global__ void __launch_bounds__(256) decode_sk_merge_kernel(const SkParams p, int grid_runs) {
+__global__ void __launch_bounds__(64) decode_sk_merge_kernel(const SkParams p, int grid_runs) {
   constexpr int DPL = D / 32;
-  pdl_wait();  // every partial of the decode grid is written and visible
+  constexpr int kBatch = 8;  // runs whose partial rows are in flight together
   const int lane = threadIdx.x & 31;
-  const int wid = blockIdx.x * 8 + (threadIdx.x >> 5);
-  if (wid >= p.batch * p.hq) return;
-  const int b = wid / p.hq, qrow = wid % p.hq;
-  const int base0 = p.indptr[0];
-  const int total = p.indptr[p.batch] - base0;
-  if (total <= 0) return;
-  const int run = cdiv(total, grid_runs);
-  const int start_b = p.indptr[b] - base0, end_b = p.indptr[b + 1] - base0;
-  if (end_b <= start_b) return;
-  const int first = start_b / run, nch = (end_b - 1) / run - first + 1;
-  if (nch <= 1) return;
-  const int slot0 = first + b;
-  // log-sum-exp of chunk c held by lane c % 32 (the first 32 stay in a register)
-  const float lse0 = lane < nch
-      ? __ldcg(p.part_lse + static_cast<int64_t>(slot0 + lane) * p.hq + qrow) : -INFINITY;
-  float M = lse0;
-  for (int c = lane + 32; c < nch; c += 32)
-    M = fmaxf(M, __ldcg(p.part_lse + static_cast<int64_t>(slot0 + c) * p.hq + qrow));
-  M = warp_max(M);
-  float acc[DPL], wsum = 0.f;
-#pragma unroll
-  for (int i = 0; i < DPL; ++i) acc[i] = 0.f;
-  if (M != -INFINITY) {
-    for (int c0 = 0; c0 < nch; c0 += 32) {
-      const int c = c0 + lane;
-      const float lc = c0 == 0 ? lse0
-          : (c < nch ? __ldcg(p.part_lse + static_cast<int64_t>(slot0 + c) * p.hq + qrow)
-                     : -INFINITY);
-      const float w = c < nch ? exp2f(lc - M) : 0.f;
-      wsum += w;
-      const int cn = min(32, nch - c0);
-#pragma unroll 4
-      for (int j = 0; j < cn; ++j) {
-        const float wj = __shfl_sync(0xffffffffu, w, j);
-        const float *src = p.part_o + (static_cast<int64_t>(slot0 + c0 + j) * p.hq + qrow) * D;
-#pragma unroll
-        for (int i = 0; i < DPL; ++i) acc[i] += wj * __ldcg(src + i * 32 + lane);
-      }
+  const int wid = blockIdx.x * 2 + (threadIdx.x >> 5);
+  int b = 0, qrow = 0, slot0 = 0, nch = 0;
+  if (wid < p.batch * p.hq) {
+    b = wid / p.hq;
+    qrow = wid % p.hq;
+    const int base0 = p.indptr[0];
+    const int total = p.indptr[p.batch] - base0;
+    const int start_b = p.indptr[b] - base0, end_b = p.indptr[b + 1] - base0;
+    if (total > 0 && end_b > start_b) {
+      const int run = cdiv(total, grid_runs);
+      const int first = start_b / run;
+      nch = (end_b - 1) / run - first + 1;
+      slot0 = first + b;
     }
   }
-  wsum = warp_sum(wsum);
+  pdl_wait();     // every partial of the decode grid is written and visible
+  pdl_trigger();  // the next kernel may get scheduled; it waits for this grid itself
+  if (nch <= 1) return;
+  const float *lse_col = p.part_lse + static_cast<int64_t>(slot0) * p.hq + qrow;
+  const float *o_col = p.part_o + (static_cast<int64_t>(slot0) * p.hq + qrow) * D + lane;
+  const int64_t o_step = static_cast<int64_t>(p.hq) * D;  // one slot
+  float M = -INFINITY, wsum = 0.f, acc[DPL];
+#pragma unroll
+  for (int i = 0; i < DPL; ++i) acc[i] = 0.f;
+  for (int c0 = 0; c0 < nch; c0 += kBatch) {
+    // lse of runs c0 .. c0+kBatch-1 (one lane each) and their rows, all in flight
+    const int cl = c0 + lane;
+    const float lc = (lane < kBatch && cl < nch) ? __ldcg(lse_col + static_cast<int64_t>(cl) * p.hq)
+                                                 : -INFINITY;
+    float v[kBatch][DPL];
+#pragma unroll
+    for (int j = 0; j < kBatch; ++j)
+#pragma unroll
+      for (int i = 0; i < DPL; ++i)
+        v[j][i] = (c0 + j < nch) ? __ldcg(o_col + (c0 + j) * o_step + i * 32) : 0.f;
+    // running rescale to the batch's max (online softmax over batches)
+    const float mb = warp_max(lc);
+    const float mn = fmaxf(M, mb);
+    if (mn == -INFINITY) continue;
+    const float corr = exp2f(M - mn);  // 0 when M = -inf
+    wsum *= corr;
+#pragma unroll
+    for (int i = 0; i < DPL; ++i) acc[i] *= corr;
+    M = mn;
+    const float w = exp2f(lc - M);  // 0 for lanes without a run
+    wsum += warp_sum(w);
+#pragma unroll
+    for (int j = 0; j < kBatch; ++j) {
+      const float wj = __shfl_sync(0xffffffffu, w, j);
+#pragma unroll
+      for (int i = 0; i < DPL; ++i) acc[i] += wj * v[j][i];
+    }
+  }
   const float inv = wsum > 0.f ? 1.f / wsum : 0.f;
   T *ob = static_cast<T *>(p.out) + (static_cast<int64_t>(b) * p.hq + qrow) * D;
 #pragma unroll
@@ -570,7 +592,7 @@ int launch_sk_t(const SkArgs &a, const CUtensorMap &map, const SkParams &p, int 
                              a.stream, map, p);
   if (e != cudaSuccess) return fail(MI_ERR_CUDA, "decode_sk_kernel launch: %s", cudaGetErrorString(e));
   const int warps = a.batch * a.hq;
-  e = launch_pdl(decode_sk_merge_kernel<T, D>, dim3((warps + 7) / 8), dim3(256), 0, a.stream, p,
+  e = launch_pdl(decode_sk_merge_kernel<T, D>, dim3((warps + 1) / 2), dim3(64), 0, a.stream, p,
                  grid);
   if (e != cudaSuccess)
     return fail(MI_ERR_CUDA, "decode_sk_merge_kernel launch: %s", cudaGetErrorString(e));
