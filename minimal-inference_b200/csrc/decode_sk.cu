@@ -16,20 +16,25 @@
 // no host plan() and can be graph-captured.
 //
 // CTA = 1 producer warp + 8 consumer warps.
-//   * Producer: walks its run 16 tokens ("tile") at a time. Page ids come
-//     from coalesced 32-wide windows of kv_indices held in registers (the
-//     next window is prefetched). For each tile it waits for a free stage,
-//     writes the stage record, and its lanes issue one 4-D TMA tensor load
-//     (cp.async.bulk.tensor, SWIZZLE_128B) per (K/V, 64-wide half of
-//     head_dim, KV head): a 16-token x 128-byte box. The stage's mbarrier
+//   * Producer: walks its run in stages of up to tps = 8/Hkv consecutive
+//     16-token tiles (so a stage is 64 KB at head_dim 128 whatever the KV
+//     head count; fewer tiles only where shared memory is short). Page ids
+//     come from coalesced 32-wide windows of kv_indices held in registers
+//     (the next window is prefetched). For each stage it waits for a free
+//     slot, writes the stage record, and its lanes issue one 4-D TMA tensor
+//     load (cp.async.bulk.tensor, SWIZZLE_128B) per (tile, K/V, 64-wide half
+//     of head_dim, KV head): a 16-token x 128-byte box. The stage's mbarrier
 //     counts the bytes.
-//   * Consumers: warp w serves KV head w / (8/Hkv) and takes every
-//     (8/Hkv)-th tile of a run segment. The group's query heads are the M
+//   * Consumers: warp w serves KV head w / (8/Hkv); the 8/Hkv warps of a
+//     head take turns over the tiles of a segment, one tile per stage at
+//     most. The group's query heads are the M
 //     rows of mma.sync m16n8k16 (S = Q K^T, O += P V, P in registers), online
 //     softmax in the exp2 domain. The 128-byte swizzle puts the 8 rows of
 //     every ldmatrix in different banks.
-//   * Warps sharing a KV head combine through shared memory (bounded
-//     mbarrier sync); all cross-warp waits are bounded, so nothing can hang.
+//   * Warps sharing a KV head combine through one shared-memory buffer: all
+//     write (hsync), then each combines its share of the query rows and
+//     releases the buffer (hdone) before any may write the next segment's
+//     partials. All cross-warp waits are bounded, so nothing can hang.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -56,7 +61,7 @@ struct SkParams {
   const void *q;
   int64_t qsb, qsh;
   int64_t num_pages;
-  int ps, hkv, group, hq, batch, subs, stages, stage_bytes;
+  int ps, hkv, group, hq, batch, subs, stages, stage_bytes, tps;
   const int32_t *indptr, *indices, *last;
   float scale_log2;
   void *out;
@@ -65,27 +70,36 @@ struct SkParams {
   unsigned *arrive;  // [batch * hkv] (reserved; the merge kernel needs no counters)
   float *part_o;     // [(grid + batch)][hq][D]
   float *part_lse;   // [(grid + batch)][hq]
-  int bar_off, rec_off, scr_off, scr_bufs;
+  int bar_off, rec_off, scr_off;
   int meta_off;  // >= 0: kv_indptr / kv_last_page_len staged in shared memory here
 };
 
 constexpr int kSmemBatch = 1024;  // requests whose metadata fits the shared-memory copy
 
+// A stage holds nt <= tps consecutive 16-token tiles of one run segment.
+// flags: 1 first stage of the segment, 2 last, 4 direct (request wholly in
+// this run); bits 8-15 per-tile bad-page mask; bits 16-19 nt; bits 20+ the
+// stage's ordinal within the segment.
 struct __align__(16) StageRec {
-  int b, tok0, kvlen, flags;  // flags: 1 first, 2 last, 4 direct, 8 bad page; ordinal << 8
+  int b, tok0, kvlen, flags;
 };
 
-template <typename T, int D, bool G16>
+template <typename T, int D, bool G16, int HKV>
 __global__ void __launch_bounds__(kThreads, 1)
     decode_sk_kernel(const __grid_constant__ CUtensorMap tmap, const SkParams p) {
   constexpr int KS = D / 16, NT = D / 8, DH = D / 64;
+  constexpr int SUBS = kNC / HKV;                         // consumer warps per KV head
+  constexpr int kBlockBytes = HKV * kTile * 128;          // one (K/V, d-half) block of a tile
+  constexpr int kTileBytes = 2 * DH * kBlockBytes;        // one 16-token tile of all heads
+  constexpr int kBoxes = 2 * DH * HKV;                    // TMA boxes per tile
   extern __shared__ unsigned char smem_raw[];
   unsigned char *smem = reinterpret_cast<unsigned char *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int S = p.stages;
   uint64_t *full = reinterpret_cast<uint64_t *>(smem + p.bar_off);
   uint64_t *empty = full + kMaxStages;
-  uint64_t *hsync = empty + kMaxStages;  // [hkv]
+  uint64_t *hsync = empty + kMaxStages;  // [hkv] all warps of a head wrote the scratch
+  uint64_t *hdone = hsync + 8;           // [hkv] all warps of a head have read it
   StageRec *recs = reinterpret_cast<StageRec *>(smem + p.rec_off);
   float *scratch = reinterpret_cast<float *>(smem + p.scr_off);
 
@@ -96,7 +110,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(&full[threadIdx.x], 1);
     mbar_init(&empty[threadIdx.x], kNC);
   }
-  if (threadIdx.x >= 32 && threadIdx.x < 32 + p.hkv) mbar_init(&hsync[threadIdx.x - 32], p.subs);
+  if (threadIdx.x >= 32 && threadIdx.x < 32 + HKV) {
+    mbar_init(&hsync[threadIdx.x - 32], SUBS);
+    mbar_init(&hdone[threadIdx.x - 32], SUBS);
+  }
   pdl_trigger();  // the merge kernel may get scheduled next to this grid
   // Launched with PDL, this grid may start while the kernel before it (the
   // append that writes this step's K/V and q) still runs. Everything up to
@@ -119,7 +136,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int32_t *ip = p.indptr, *lp = p.last;
   if (p.meta_off >= 0) {
     int32_t *s_ip = reinterpret_cast<int32_t *>(smem + p.meta_off);
-    int32_t *s_lp = s_ip + kSmemBatch + 1;
+    int32_t *s_lp = s_ip + p.batch + 1;
     for (int i = threadIdx.x; i <= p.batch; i += blockDim.x) {
       s_ip[i] = p.indptr[i];
       if (i < p.batch) s_lp[i] = p.last[i];
@@ -133,7 +150,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int total = ip[p.batch] - base0;
   const int run = total > 0 ? cdiv(total, G) : 1;  // pages per CTA
 
-  const int block_bytes = p.hkv * kTile * 128;  // one (K/V, d-half) block of a stage
+  constexpr int block_bytes = kBlockBytes;
 
   // =========================== producer warp ==============================
   if (warp == kNC) {
@@ -165,41 +182,59 @@ __global__ void __launch_bounds__(kThreads, 1)
         // A segment without tokens (last_page_len 0) still gets one fully
         // masked tile, so its partial and its merge arrival exist.
         const int ntiles = tok_end > tok_begin ? cdiv(tok_end - tok_begin, kTile) : 1;
-        for (int j = 0; j < ntiles; ++j) {
-          const int tok0 = tok_begin + j * kTile;
-          const int gpos = start_b + tok0 / p.ps;
-          while (gpos >= wbase + 32) {
+        constexpr int nbox = kBoxes;  // nbox * tps <= 32
+        for (int j0 = 0, ord = 0; j0 < ntiles; j0 += p.tps, ++ord) {
+          const int nt = min(p.tps, ntiles - j0);
+          const int tok0 = tok_begin + j0 * kTile;
+          const int gpos0 = start_b + tok0 / p.ps;  // page position of the stage's first tile
+          while (gpos0 >= wbase + 32) {
             wbase += 32;
             pw = pwn;
             pwn = (wbase + 32 + lane < total) ? p.indices[base0 + wbase + 32 + lane] : -1;
           }
-          const int page = __shfl_sync(0xffffffffu, pw, gpos - wbase);
-          const bool bad = page < 0 || page >= p.num_pages;
+          // lane -> (tile t, K/V, d-half, head); a stage spans at most 9 pages,
+          // so its page ids sit in the current or the next window
+          const int t = lane / nbox, r = lane % nbox;
+          const int ttok = tok0 + t * kTile;
+          int page;
+          bool mine, bad;
+          int badmask = 0;
+          if constexpr (SUBS == 1) {  // one tile per stage, one page id for all lanes
+            page = __shfl_sync(0xffffffffu, pw, gpos0 - wbase);
+            mine = true;
+            bad = page < 0 || page >= p.num_pages;
+            badmask = bad ? 1 : 0;
+          } else {
+            const int off = start_b + ttok / p.ps - wbase;
+            const int pa = __shfl_sync(0xffffffffu, pw, off & 31);
+            const int pb = __shfl_sync(0xffffffffu, pwn, off & 31);
+            page = off < 32 ? pa : pb;
+            mine = t < nt;
+            bad = mine && (page < 0 || page >= p.num_pages);
+            const unsigned badl = __ballot_sync(0xffffffffu, bad);
+            for (int tt = 0; tt < nt; ++tt) badmask |= ((badl >> (tt * nbox)) & 1u) << tt;
+          }
+          // everything but the issue itself is ready before the wait for a free slot
           const int s = k % S;
+          const int flags = (j0 == 0 ? 1 : 0) | (j0 + nt >= ntiles ? 2 : 0) | (direct ? 4 : 0) |
+                            (badmask << 8) | (nt << 16) | ((ord & 2047) << 20);
+          const uint32_t tx = static_cast<uint32_t>(nt - __popc(badmask)) * kTileBytes;
+          const int h = r % HKV, rest = r / HKV;
+          const int dh = rest % DH, which = rest / DH;
+          unsigned char *dst = smem + s * p.stage_bytes + t * kTileBytes +
+                               (which * DH + dh) * block_bytes + h * (kTile * 128);
+          const int row = ttok % p.ps, plane = page * 2 + which;
           if (!__all_sync(0xffffffffu, mbar_wait_bounded(&empty[s], ((k / S) & 1) ^ 1))) {
             ok_run = false;
             break;
           }
-          int flags = (j == 0 ? 1 : 0) | (j == ntiles - 1 ? 2 : 0) | (direct ? 4 : 0) |
-                      (bad ? 8 : 0) | (j << 8);
           if (lane == 0) {
             recs[s] = StageRec{b, tok0, kvlen, flags};
-            mbar_arrive_expect_tx(&full[s], bad ? 0u : static_cast<uint32_t>(p.stage_bytes));
-            if (bad) flag(p.status, MI_STATUS_BAD_PAGE);
+            mbar_arrive_expect_tx(&full[s], tx);
+            if (badmask) flag(p.status, MI_STATUS_BAD_PAGE);
           }
           __syncwarp();
-          if (!bad) {
-            // lane -> (kv, d-half, head)
-            const int nbox = 2 * DH * p.hkv;
-            if (lane < nbox) {
-              const int h = lane % p.hkv, rest = lane / p.hkv;
-              const int dh = rest % DH, which = rest / DH;
-              unsigned char *dst = smem + s * p.stage_bytes + (which * DH + dh) * block_bytes +
-                                   h * (kTile * 128);
-              tma_load_4d(dst, &tmap, dh * 64, h, tok0 % p.ps, page * 2 + which, &full[s],
-                          policy);
-            }
-          }
+          if (mine && !bad) tma_load_4d(dst, &tmap, dh * 64, h, row, plane, &full[s], policy);
           ++k;
         }
         pos = sub_hi;
@@ -230,7 +265,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   // =========================== consumer warps =============================
   pdl_wait();  // q, out, lse and the workspace are the predecessor's to finish with
-  const int subs = p.subs;
+  constexpr int subs = SUBS;
   const int h = warp / subs, sw = warp % subs;
   const int gid = lane >> 2, tq = lane & 3;
 
@@ -285,11 +320,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       m0 = m1 = -INFINITY;
       l0 = l1 = 0.f;
     }
-    if (((flags >> 8) % subs) == sw) {
-      unsigned char *st = smem + s * p.stage_bytes;
+    // this warp's tile of the stage: the head's warps take the segment's
+    // tiles in turn (tile index ord * tps + t goes to warp (ord * tps + t) % subs)
+    const int nt = (flags >> 16) & 15, ord = flags >> 20;
+    const int t = subs == 1 ? 0 : (sw - (ord * p.tps) % subs + subs) % subs;
+    if (t < nt) {
+      unsigned char *st = smem + s * p.stage_bytes + t * kTileBytes;
       const uint32_t kbase = smem_u32(st) + h * (kTile * 128);
       const uint32_t vbase = kbase + DH * block_bytes;
-      const int nvalid = (flags & 8) ? 0 : rec.kvlen - rec.tok0;
+      const int nvalid = ((flags >> (8 + t)) & 1) ? 0 : rec.kvlen - (rec.tok0 + t * kTile);
       if (nvalid < kTile) {
         // rows past the request (or of a bad page) may hold anything: zero
         // this head's V rows there so P = 0 never meets a NaN
@@ -397,10 +436,16 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     if (!(flags & 2)) continue;
     // ---- end of a run segment: combine the warps of this KV head ----------
-    const int buf = (p.scr_bufs == 2) ? (segments & 1) : 0;
+    // Before overwriting its scratch row block, a warp waits until all of
+    // the head's warps have read the previous segment's.
+    if (subs > 1 && segments > 0 &&
+        !__all_sync(0xffffffffu, mbar_wait_bounded(&hdone[h], (segments - 1) & 1))) {
+      timed_out = true;
+      break;
+    }
     ++segments;
     const int RS = p.group * (D + 2);  // floats per warp in the scratch
-    float *mine = scratch + (static_cast<size_t>(buf) * kNC + warp) * RS;
+    float *mine = scratch + static_cast<size_t>(warp) * RS;
     {
       float ls0 = l0 + __shfl_xor_sync(0xffffffffu, l0, 1);
       ls0 += __shfl_xor_sync(0xffffffffu, ls0, 2);
@@ -433,15 +478,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         timed_out = true;
         break;
       }
-      if (sw != 0) continue;
     }
-    // warp (h, 0): rows h*group .. h*group+group-1 of request rec.b
+    // warp (h, sw): rows h*group + r, r = sw, sw + subs, ... of request rec.b
     const int b = rec.b;
     const bool direct = flags & 4;
     constexpr int DPL = D / 32;
-    const float *first = scratch + (static_cast<size_t>(buf) * kNC + h * subs) * RS;
+    const float *first = scratch + static_cast<size_t>(h * subs) * RS;
     const int slot = cta + b;
-    for (int r = 0; r < p.group; ++r) {
+    for (int r = sw; r < p.group; r += subs) {
       float M = -INFINITY;
       for (int j = 0; j < subs; ++j) M = fmaxf(M, first[j * RS + r * (D + 2) + D]);
       float acc[DPL], L = 0.f;
@@ -470,6 +514,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int i = 0; i < DPL; ++i) po[i * 32 + lane] = acc[i] * inv;
         if (lane == 0) p.part_lse[slot * p.hq + qrow] = L > 0.f ? M + __log2f(L) : -INFINITY;
       }
+    }
+    if (subs > 1) {  // this warp's reads are done: the scratch may be reused once all are
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&hdone[h]);
     }
   }
   if (timed_out && lane == 0) flag(p.status, MI_STATUS_TIMEOUT);
@@ -552,43 +600,55 @@ __global__ void __launch_bounds__(64) decode_sk_merge_kernel(const SkParams p, i
 // host side: tensor maps (cached per pool), launch
 // ---------------------------------------------------------------------------
 struct SkLayout {
-  int stages, stage_bytes, bar_off, rec_off, scr_off, scr_bufs, meta_off, smem;
+  int stages, stage_bytes, tps, bar_off, rec_off, scr_off, meta_off, smem;
 };
 
+// Shared memory: stages of tps tiles, barriers (full/empty per stage,
+// hsync/hdone per KV head), stage records, the combine scratch (one
+// group x (D+2) fp32 block per consumer warp) and, for batches up to
+// kSmemBatch, a copy of kv_indptr / kv_last_page_len. tps is the largest
+// power of two <= 8/Hkv that still leaves three stages (two at the least).
 bool sk_layout(int hkv, int d, int group, int batch, SkLayout *L) {
   const int subs = kNC / hkv;
-  L->stage_bytes = 2 * hkv * kTile * d * 2;
-  L->scr_bufs = subs > 1 ? 2 : 1;
-  const int scr = L->scr_bufs * kNC * group * (d + 2) * 4;
-  const int meta = batch <= kSmemBatch ? (2 * kSmemBatch + 4) * 4 : 0;
-  const int fixed =
-      1024 /*align slack*/ + (2 * kMaxStages + 8) * 8 + kMaxStages * 16 + scr + meta;
-  int s = (kSmemLimit - fixed) / L->stage_bytes;
-  if (s > kMaxStages) s = kMaxStages;
-  if (s < 2) return false;
-  L->stages = s;
-  L->bar_off = s * L->stage_bytes;
-  L->rec_off = L->bar_off + (2 * kMaxStages + 8) * 8;
-  L->scr_off = L->rec_off + kMaxStages * 16;
-  L->meta_off = meta ? L->scr_off + scr : -1;
-  L->smem = L->scr_off + scr + meta + 1024;
-  return L->smem <= kSmemLimit;
+  const int tile_bytes = 2 * hkv * kTile * d * 2;
+  const int scr = kNC * group * (d + 2) * 4;
+  const int meta = batch <= kSmemBatch ? ((2 * batch + 4) * 4 + 15) / 16 * 16 : 0;
+  const int ctrl = (2 * kMaxStages + 16) * 8 + kMaxStages * 16;
+  const int fixed = 1024 /*align slack*/ + ctrl + scr + meta;
+  for (int min_stages = 3; min_stages >= 2; --min_stages) {
+    for (int tps = subs; tps >= 1; tps >>= 1) {
+      const int stage_bytes = tps * tile_bytes;
+      int st = (kSmemLimit - fixed) / stage_bytes;
+      if (st > kMaxStages) st = kMaxStages;
+      if (st < min_stages) continue;
+      L->tps = tps;
+      L->stages = st;
+      L->stage_bytes = stage_bytes;
+      L->bar_off = st * stage_bytes;
+      L->rec_off = L->bar_off + (2 * kMaxStages + 16) * 8;
+      L->scr_off = L->rec_off + kMaxStages * 16;
+      L->meta_off = meta ? L->scr_off + scr : -1;
+      L->smem = L->scr_off + scr + meta + 1024;
+      return L->smem <= kSmemLimit;
+    }
+  }
+  return false;
 }
 
-template <typename T, int D, bool G16>
+template <typename T, int D, bool G16, int HKV>
 int launch_sk_t(const SkArgs &a, const CUtensorMap &map, const SkParams &p, int grid,
                 int smem) {
   static unsigned long long attr_set = 0;
   int dev = 0;
   cudaGetDevice(&dev);
   if (!(attr_set >> (dev & 63) & 1ull)) {
-    if (cudaFuncSetAttribute(decode_sk_kernel<T, D, G16>,
+    if (cudaFuncSetAttribute(decode_sk_kernel<T, D, G16, HKV>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize,
                              kSmemLimit) != cudaSuccess)
       return check_launch("decode_sk_kernel smem attribute");
     attr_set |= 1ull << (dev & 63);
   }
-  cudaError_t e = launch_pdl(decode_sk_kernel<T, D, G16>, dim3(grid), dim3(kThreads), smem,
+  cudaError_t e = launch_pdl(decode_sk_kernel<T, D, G16, HKV>, dim3(grid), dim3(kThreads), smem,
                              a.stream, map, p);
   if (e != cudaSuccess) return fail(MI_ERR_CUDA, "decode_sk_kernel launch: %s", cudaGetErrorString(e));
   const int warps = a.batch * a.hq;
@@ -597,6 +657,16 @@ int launch_sk_t(const SkArgs &a, const CUtensorMap &map, const SkParams &p, int 
   if (e != cudaSuccess)
     return fail(MI_ERR_CUDA, "decode_sk_merge_kernel launch: %s", cudaGetErrorString(e));
   return check_launch("decode_sk_merge_kernel");
+}
+
+template <typename T, int D, bool G16>
+int launch_sk_h(const SkArgs &a, const CUtensorMap &map, const SkParams &p, int grid, int smem) {
+  switch (a.hkv) {
+    case 1: return launch_sk_t<T, D, G16, 1>(a, map, p, grid, smem);
+    case 2: return launch_sk_t<T, D, G16, 2>(a, map, p, grid, smem);
+    case 4: return launch_sk_t<T, D, G16, 4>(a, map, p, grid, smem);
+    default: return launch_sk_t<T, D, G16, 8>(a, map, p, grid, smem);
+  }
 }
 
 }  // namespace
@@ -641,6 +711,7 @@ int launch_decode_sk(const SkArgs &a) {
   p.subs = kNC / a.hkv;
   p.stages = L.stages;
   p.stage_bytes = L.stage_bytes;
+  p.tps = L.tps;
   p.indptr = a.indptr;
   p.indices = a.indices;
   p.last = a.last;
@@ -655,21 +726,20 @@ int launch_decode_sk(const SkArgs &a) {
   p.bar_off = L.bar_off;
   p.rec_off = L.rec_off;
   p.scr_off = L.scr_off;
-  p.scr_bufs = L.scr_bufs;
   p.meta_off = L.meta_off;
   const bool g16 = group > 8;
   if (a.dtype == MI_DTYPE_BF16) {
     if (a.d == 128)
-      return g16 ? launch_sk_t<__nv_bfloat16, 128, true>(a, map, p, grid, L.smem)
-                 : launch_sk_t<__nv_bfloat16, 128, false>(a, map, p, grid, L.smem);
-    return g16 ? launch_sk_t<__nv_bfloat16, 64, true>(a, map, p, grid, L.smem)
-               : launch_sk_t<__nv_bfloat16, 64, false>(a, map, p, grid, L.smem);
+      return g16 ? launch_sk_h<__nv_bfloat16, 128, true>(a, map, p, grid, L.smem)
+                 : launch_sk_h<__nv_bfloat16, 128, false>(a, map, p, grid, L.smem);
+    return g16 ? launch_sk_h<__nv_bfloat16, 64, true>(a, map, p, grid, L.smem)
+               : launch_sk_h<__nv_bfloat16, 64, false>(a, map, p, grid, L.smem);
   }
   if (a.d == 128)
-    return g16 ? launch_sk_t<__half, 128, true>(a, map, p, grid, L.smem)
-               : launch_sk_t<__half, 128, false>(a, map, p, grid, L.smem);
-  return g16 ? launch_sk_t<__half, 64, true>(a, map, p, grid, L.smem)
-             : launch_sk_t<__half, 64, false>(a, map, p, grid, L.smem);
+    return g16 ? launch_sk_h<__half, 128, true>(a, map, p, grid, L.smem)
+               : launch_sk_h<__half, 128, false>(a, map, p, grid, L.smem);
+  return g16 ? launch_sk_h<__half, 64, true>(a, map, p, grid, L.smem)
+             : launch_sk_h<__half, 64, false>(a, map, p, grid, L.smem);
 }
 
 }  // namespace mi
