@@ -190,11 +190,8 @@ def model_decode(dev, batch=32, out_tokens=50, seed=3):
     import torch
     from mi_b200.model import PRESETS, Model
     from mi_b200.scheduler import Request, Scheduler
-    from mi_b200.weights import init_random_weights
     cfg = PRESETS["mistral-7b"]
-    model = Model(cfg).to(device=dev, dtype=torch.bfloat16)
-    init_random_weights(model, seed, generator_device="cuda")
-    model.eval().prepare()
+    model = Model.create(cfg, dev, torch.bfloat16, seed=seed)
     rng = np.random.default_rng(seed)
     lens = rng.integers(128, 1025, batch).tolist()
     prompts = [rng.integers(0, cfg.vocab_size, n).tolist() for n in lens]
@@ -232,6 +229,107 @@ def model_decode(dev, batch=32, out_tokens=50, seed=3):
 
 
 # ---------------------------------------------------------------------------
+def run_tp_decode(args):
+    """Qwen2.5-72B-shape continuous-batching decode with
+    tensor parallelism over the N GPUs of the launch (one rank per GPU, NCCL).
+
+    64 requests, prompts U[512, 4096] of random ids (seeded, the same on every
+    rank), 129 output tokens each (1 from prefill + 128 decode steps), page
+    size 16, max_seq_len 4224, greedy sampling, CUDA-graph decode with the two
+    all-reduces per layer captured in the graph. Random bf16 weights
+    (``Model.create``: each rank keeps its slices of the same seeded tensors).
+    T2T follows the reference's definition (per request, time between its
+    first and last token over tokens - 1, averaged); every timing is the max
+    over ranks. ``--model`` swaps in a smaller preset for quick checks.
+    """
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    from mi_b200.model import PRESETS, Model
+    from mi_b200.scheduler import Request, Scheduler
+
+    rank, world, local = dist_env()
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+    group = dist.group.WORLD if world > 1 else None
+    name = args.model or "qwen2.5-72b"
+    cfg = PRESETS[name]
+    batch, lo, hi, steps = args.batch or 64, 512, 4096, args.decode_steps or 128
+    t0 = time.perf_counter()
+    model = Model.create(cfg, dev, torch.bfloat16, seed=5, tp_rank=rank, tp_size=world,
+                         tp_group=group)
+    torch.cuda.synchronize()
+    init_s = time.perf_counter() - t0
+    rng = np.random.default_rng(5)
+    lens = rng.integers(lo, hi + 1, batch).tolist()
+    prompts = [rng.integers(0, cfg.vocab_size, n).tolist() for n in lens]
+    t0 = time.perf_counter()
+    sched = Scheduler(model, cfg, dev, torch.bfloat16, max_batch_size=batch,
+                      max_seq_len=hi + steps, page_size=16, eos_token_ids=set(),
+                      max_prefill_tokens=16384)
+    torch.cuda.synchronize()
+    capture_s = time.perf_counter() - t0
+
+    def max_over_ranks(vals):
+        t = torch.tensor(vals, dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return t.tolist()
+
+    reqs = [Request(f"r{i}", p, steps + 1, 0.0) for i, p in enumerate(prompts)]
+    for r in reqs:
+        sched.submit_request(r)
+    clocks = ClockSampler(local)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier(device_ids=[local])
+    t0 = time.perf_counter()
+    sched.step()                                   # admit + prefill all + first decode
+    torch.cuda.synchronize()
+    first_s = time.perf_counter() - t0
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record()
+    n_dec = 0
+    while sched.active_requests or sched.waiting_queue:
+        sched.step()
+        n_dec += 1
+    ev1.record()
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    dec_ms = ev0.elapsed_time(ev1) / max(n_dec, 1)
+    t2t = statistics.mean((r.last_token_time - r.prefill_done_time)
+                          / (len(r.generated_tokens) - 1) for r in reqs) * 1e3
+    t2t, dec_ms, first_s, init_s, capture_s = max_over_ranks(
+        [t2t, dec_ms, first_s, init_s, capture_s])
+    ok = all(len(r.generated_tokens) == steps + 1 for r in reqs)
+    sched.close()
+    del sched, model
+    if world > 1:
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    line = {
+        "metric": f"{name} decode tok/s @B={batch}, tensor parallel (config 5)",
+        "value": round(batch / (t2t / 1e3), 1), "unit": "tok/s", "n_gpus": world,
+        "steps": steps, "warmup": 0, "ms_per_step": round(dec_ms, 3), "t2t_ms": round(t2t, 3),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic",
+        "config": {"workload": "BASELINE config 5: continuous-batching decode, all requests "
+                               "admitted at once, greedy", "model": name,
+                   "global_batch": batch, "seq_len": f"prompts U[{lo},{hi}] + {steps} decode",
+                   "parallelism": f"tp{world}", "page_size": 16,
+                   "weights": "random N(0,0.02) bf16"},
+        "first_step_s (prefill of all + 1 decode)": round(first_s, 3),
+        "model_init_s": round(init_s, 2), "graph_capture_s": round(capture_s, 2),
+        "decode_steps_timed": n_dec, "all_requests_complete": ok, "clocks": clk,
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------
 def parse_args():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -244,6 +342,12 @@ def parse_args():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-model", action="store_true",
                     help="skip the Mistral-7B-shape decode measurement (config 3)")
+    ap.add_argument("--workload", choices=["config2", "config5"], default="config2",
+                    help="config5: Qwen2.5-72B tensor-parallel decode over the launch's GPUs")
+    ap.add_argument("--model", default=None, help="config5: model preset (default qwen2.5-72b)")
+    ap.add_argument("--batch", type=int, default=None, help="config5: requests (default 64)")
+    ap.add_argument("--decode-steps", type=int, default=None,
+                    help="config5: decode steps per request (default 128)")
     return ap.parse_args()
 
 
@@ -295,6 +399,9 @@ def main():
     args = parse_args()
     if args.impl == "reference":
         run_reference(args)
+        return
+    if args.workload == "config5":
+        run_tp_decode(args)
         return
     import torch
     import torch.distributed as dist

@@ -18,6 +18,14 @@ gate/up run as one GEMM each over fused weight views. Each residual add runs
 fused with the RMSNorm that follows it, and SiLU(gate) * up is one kernel
 (``glue``), so a decoder layer is five GEMMs, two attention-path launches and
 three glue launches.
+
+Tensor parallelism (``tp_size > 1``, one process per GPU over NCCL): each rank
+holds ``Hq/tp`` query heads and ``Hkv/tp`` KV heads (its own page pools, the
+same page tables on every rank), ``intermediate/tp`` MLP columns and
+``vocab/tp`` rows of the LM head. Q/K/V and gate/up are column-parallel;
+``o_proj`` and ``down_proj`` are row-parallel and followed by one all-reduce
+each, inside the decode CUDA graph; the logits are all-gathered at the end.
+Attention needs no exchange: GQA groups never straddle ranks.
 """
 from __future__ import annotations
 
@@ -26,6 +34,7 @@ import json
 import os
 
 import torch
+import torch.distributed as dist
 import torch.nn as nn
 import torch.nn.functional as F
 
@@ -184,12 +193,19 @@ class MLP(nn.Module):
 
 
 class DecoderLayer(nn.Module):
-    def __init__(self, config: ModelConfig, **shard):
+    def __init__(self, config: ModelConfig, tp_size: int = 1, tp_group=None, **shard):
         super().__init__()
         self.input_layernorm = RMSNorm(config.hidden_size, config.rms_norm_eps)
         self.self_attn = Attention(config, shard.get("num_heads"), shard.get("num_kv_heads"))
         self.post_attention_layernorm = RMSNorm(config.hidden_size, config.rms_norm_eps)
         self.mlp = MLP(config, shard.get("intermediate_size"))
+        self.tp_size, self.tp_group = tp_size, tp_group
+
+    def _reduce(self, x: torch.Tensor) -> torch.Tensor:
+        """Sum of the row-parallel partial outputs over the tensor-parallel ranks."""
+        if self.tp_size > 1:
+            dist.all_reduce(x, group=self.tp_group)
+        return x
 
     def forward(self, x, cos, sin, mask, kv_cache=None, position_ids=None, attn_backend=None):
         """Reference signature (model.py:322-343); returns the new residual."""
@@ -204,21 +220,72 @@ class DecoderLayer(nn.Module):
         (None for the first layer); the add runs fused into this layer's input
         RMSNorm. Returns this layer's MLP output, likewise not yet added."""
         y = add_rmsnorm(pending, h, self.input_layernorm.weight, self.input_layernorm.eps)
-        a = self.self_attn(y, None, None, None, None, position_ids, attn_backend)
+        a = self._reduce(self.self_attn(y, None, None, None, None, position_ids, attn_backend))
         y = add_rmsnorm(a, h, self.post_attention_layernorm.weight,
                         self.post_attention_layernorm.eps)
-        return self.mlp(y)
+        return self._reduce(self.mlp(y))
+
+
+def tp_shard_sizes(config: ModelConfig, tp_size: int) -> dict:
+    """Per-rank head / column counts; raises if ``tp_size`` does not divide them."""
+    dims = {"num_heads": config.num_attention_heads, "num_kv_heads": config.num_key_value_heads,
+            "intermediate_size": config.intermediate_size, "vocab_size": config.vocab_size}
+    for k, v in dims.items():
+        if v % tp_size:
+            raise ValueError(f"tensor parallel size {tp_size} does not divide {k}={v}")
+    return {k: v // tp_size for k, v in dims.items()}
+
+
+def tp_shard_spec(name: str):
+    """``(dim, kind)`` of parameter ``name`` under tensor parallelism, or None
+    if every rank holds all of it. kind: "col" (output rows split) or "row"
+    (input columns split, output summed by all-reduce)."""
+    leaf = name.split(".")
+    if len(leaf) >= 4 and leaf[0] == "layers":
+        mod, proj = leaf[2], leaf[3]
+        if mod == "self_attn" and proj in ("q_proj", "k_proj", "v_proj"):
+            return 0, "col"
+        if mod == "self_attn" and proj == "o_proj" and leaf[-1] == "weight":
+            return 1, "row"
+        if mod == "mlp" and proj in ("gate_proj", "up_proj"):
+            return 0, "col"
+        if mod == "mlp" and proj == "down_proj":
+            return 1, "row"
+    if name == "lm_head.weight":
+        return 0, "col"
+    return None
+
+
+def gather_vocab_logits(local: torch.Tensor, tp_size: int, group=None) -> torch.Tensor:
+    """``[..., V/tp]`` vocab shards of every rank -> ``[..., V]`` on every rank."""
+    if tp_size == 1:
+        return local
+    lead, vl = local.shape[:-1], local.shape[-1]
+    flat = local.reshape(-1, vl).contiguous()
+    out = torch.empty(tp_size * flat.shape[0], vl, dtype=flat.dtype, device=flat.device)
+    dist.all_gather_into_tensor(out, flat, group=group)
+    full = out.view(tp_size, flat.shape[0], vl).permute(1, 0, 2).reshape(flat.shape[0], -1)
+    return full.reshape(*lead, tp_size * vl)
 
 
 class Model(nn.Module):
-    def __init__(self, config: ModelConfig):
+    def __init__(self, config: ModelConfig, tp_rank: int = 0, tp_size: int = 1, tp_group=None):
         super().__init__()
         self.config = config
+        self.tp_rank, self.tp_size, self.tp_group = tp_rank, tp_size, tp_group
+        shard = {}
+        vocab_local = config.vocab_size
+        if tp_size > 1:
+            sizes = tp_shard_sizes(config, tp_size)
+            shard = {k: sizes[k] for k in ("num_heads", "num_kv_heads", "intermediate_size")}
+            vocab_local = sizes["vocab_size"]
         self.embed_tokens = nn.Embedding(config.vocab_size, config.hidden_size)
-        self.layers = nn.ModuleList([DecoderLayer(config) for _ in range(config.num_hidden_layers)])
+        self.layers = nn.ModuleList([DecoderLayer(config, tp_size, tp_group, **shard)
+                                     for _ in range(config.num_hidden_layers)])
         self.norm = RMSNorm(config.hidden_size, config.rms_norm_eps)
         self.lm_head = (None if config.tie_word_embeddings else
-                        nn.Linear(config.hidden_size, config.vocab_size, bias=False))
+                        nn.Linear(config.hidden_size, vocab_local, bias=False))
+        self.vocab_local = vocab_local
         # fp32 tables built exactly as model.py:79-89, cast with the model
         cos, sin = rope_tables(config.head_dim, config.max_position_embeddings,
                                config.rope_theta)
@@ -231,6 +298,34 @@ class Model(nn.Module):
             layer.self_attn.fuse()
             layer.mlp.fuse()
         return self
+
+    @classmethod
+    def create(cls, config: ModelConfig, device, dtype: torch.dtype, seed: int | None = None,
+               tp_rank: int = 0, tp_size: int = 1, tp_group=None) -> "Model":
+        """Allocate the model (this rank's shard) directly on ``device`` in
+        ``dtype`` -- no host copy, so 70B-class shapes need no host memory --
+        optionally fill it with the seeded random weights of
+        ``weights.init_random_weights`` (each rank keeps its slices of the same
+        full tensors), and fuse the GEMM weights."""
+        from .weights import init_random_weights
+
+        with torch.device("meta"):
+            model = cls(config, tp_rank, tp_size, tp_group)
+        model = model.to(dtype=dtype).to_empty(device=device)
+        cos, sin = rope_tables(config.head_dim, config.max_position_embeddings,
+                               config.rope_theta)
+        model.cos_cached = cos.to(dtype).to(device)
+        model.sin_cached = sin.to(dtype).to(device)
+        if seed is not None:
+            init_random_weights(model, seed, generator_device=torch.device(device).type)
+        return model.eval().prepare()
+
+    def _lm_head_weight(self) -> torch.Tensor:
+        if self.lm_head is not None:
+            return self.lm_head.weight
+        w = self.embed_tokens.weight               # tied: this rank's vocab rows
+        return w if self.tp_size == 1 else w.narrow(0, self.tp_rank * self.vocab_local,
+                                                    self.vocab_local)
 
     def forward(self, input_ids, kv_caches=None, position_ids=None, attention_mask=None,
                 attn_backend=None, *, logits_rows: torch.Tensor | None = None):
@@ -249,6 +344,5 @@ class Model(nn.Module):
         h = add_rmsnorm(pending, h, self.norm.weight, self.norm.eps)
         if logits_rows is not None:
             h = h.reshape(-1, h.shape[-1])[logits_rows].unsqueeze(0)
-        if self.lm_head is not None:
-            return self.lm_head(h)
-        return F.linear(h, self.embed_tokens.weight)
+        return gather_vocab_logits(F.linear(h, self._lm_head_weight()), self.tp_size,
+                                   self.tp_group)

@@ -15,8 +15,10 @@ import torch
 def rope_tables(head_dim: int, max_pos: int, theta: float,
                 dtype: torch.dtype = torch.float32, device="cpu"):
     """``(cos, sin)`` of shape ``[max_pos, head_dim]`` in ``dtype`` on ``device``."""
-    inv_freq = 1.0 / (theta ** (torch.arange(0, head_dim, 2).float() / head_dim))
-    t = torch.arange(max_pos, dtype=torch.float32)
+    # built on the host whatever the default device is (e.g. a meta-device
+    # model construction)
+    inv_freq = 1.0 / (theta ** (torch.arange(0, head_dim, 2, device="cpu").float() / head_dim))
+    t = torch.arange(max_pos, dtype=torch.float32, device="cpu")
     freqs = torch.outer(t, inv_freq)
     emb = torch.cat([freqs, freqs], dim=-1)
     cos, sin = emb.cos(), emb.sin()

@@ -225,7 +225,8 @@ class Scheduler:
                  max_seq_len: int = 4096, page_size: int = 16,
                  eos_token_ids: set[int] | None = None, use_flashinfer: bool = True,
                  use_cuda_graph: bool = True, teacher_tokens: dict | None = None,
-                 num_kv_heads: int | None = None, num_heads: int | None = None):
+                 num_kv_heads: int | None = None, num_heads: int | None = None,
+                 max_prefill_tokens: int = 32768):
         global EOS_TOKEN_IDS
         if eos_token_ids is not None:
             EOS_TOKEN_IDS = eos_token_ids
@@ -235,8 +236,10 @@ class Scheduler:
         self.model, self.config = model, config
         self.device, self.dtype = device, dtype
         self.max_batch_size, self.max_seq_len, self.page_size = max_batch_size, max_seq_len, page_size
-        self.num_heads = num_heads or config.num_attention_heads
-        self.num_kv_heads = num_kv_heads or config.num_key_value_heads
+        attn0 = model.layers[0].self_attn   # this rank's heads under tensor parallelism
+        self.num_heads = num_heads or attn0.num_heads
+        self.num_kv_heads = num_kv_heads or attn0.num_kv_heads
+        self.max_prefill_tokens = max_prefill_tokens
         self.kv_cache = PagedKVCache(config, max_batch_size, max_seq_len, page_size, device, dtype,
                                      num_kv_heads=self.num_kv_heads)
         ws = 256 * 1024 * 1024
@@ -277,6 +280,15 @@ class Scheduler:
         self.new_request_event.set()
         if self._thread:
             self._thread.join()
+
+    def close(self) -> None:
+        """Release the decode CUDA graphs (they hold NCCL work under tensor
+        parallelism and must go before the process group is destroyed)."""
+        torch.cuda.synchronize(self.device)
+        for r in self._graph_runners.values():
+            r.graph = None
+            r.logits = None
+        self._graph_runners.clear()
 
     def submit_request(self, request: Request) -> None:
         with self.lock:
@@ -320,11 +332,22 @@ class Scheduler:
             self.kv_cache.slot_alloc(slots, counts, sum(n for _, n in admitted))
 
     # ---- prefill (scheduler.py:643-752), batched -----------------------------
-    @torch.inference_mode()
     def _prefill_new_requests(self) -> None:
         reqs = [r for r in self.active_requests if r.status == RequestStatus.PREFILLING]
-        if not reqs:
-            return
+        # one ragged forward per group of at most max_prefill_tokens prompt
+        # tokens (a longer prompt goes alone), in admission order
+        group, n = [], 0
+        for r in reqs:
+            if group and n + len(r.input_ids) > self.max_prefill_tokens:
+                self._prefill_batch(group)
+                group, n = [], 0
+            group.append(r)
+            n += len(r.input_ids)
+        if group:
+            self._prefill_batch(group)
+
+    @torch.inference_mode()
+    def _prefill_batch(self, reqs: list) -> None:
         dev = self.device
         lens = [len(r.input_ids) for r in reqs]
         total = sum(lens)

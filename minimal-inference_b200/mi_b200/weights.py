@@ -22,18 +22,30 @@ def init_random_weights(model: torch.nn.Module, seed: int, std: float = 0.02,
 
     Parameters are visited in sorted-name order; each draws
     ``torch.randn(shape, generator=g) * std`` in fp32 from one generator seeded
-    with ``seed`` and is then cast into the parameter's dtype/device.
+    with ``seed`` and is then cast into the parameter's dtype/device. On a
+    tensor-parallel shard (``model.tp_size > 1``) each split parameter draws
+    its full shape and keeps the rank's slice, so every rank holds slices of
+    the very tensors an unsharded model gets.
     ``generator_device="cuda"`` draws on the GPU instead (fast for 7B+ shapes;
     not bit-identical to the CPU stream).
     """
+    from .model import tp_shard_spec
+
+    tp_size, tp_rank = getattr(model, "tp_size", 1), getattr(model, "tp_rank", 0)
     g = torch.Generator(device=generator_device)
     g.manual_seed(seed)
     for name, p in sorted(model.named_parameters(), key=lambda kv: kv[0]):
         if name.endswith("norm.weight"):
             p.fill_(1.0)
             continue
-        w = torch.randn(tuple(p.shape), generator=g, dtype=torch.float32,
-                        device=generator_device)
+        spec = tp_shard_spec(name) if tp_size > 1 else None
+        shape = list(p.shape)
+        if spec is not None:  # draw the full tensor, keep this rank's slice
+            shape[spec[0]] *= tp_size
+        w = torch.randn(tuple(shape), generator=g, dtype=torch.float32, device=generator_device)
+        if spec is not None:
+            n = p.shape[spec[0]]
+            w = w.narrow(spec[0], tp_rank * n, n)
         w.mul_(std)
         p.copy_(w)
         del w
