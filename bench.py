@@ -330,6 +330,174 @@ def run_tp_decode(args):
 
 
 # ---------------------------------------------------------------------------
+DECODE_SHAPES = [  # (batch, Q heads, KV heads, ctx lo, ctx hi, note)
+    (32, 32, 8, 256, 4096, "config 2"),
+    (64, 32, 8, 512, 4096, ""),
+    (64, 64, 8, 512, 4096, "Qwen2.5-72B, one GPU's worth of heads"),
+    (64, 32, 4, 512, 4096, "Qwen2.5-72B at TP 2"),
+    (64, 16, 2, 512, 4096, "Qwen2.5-72B at TP 4"),
+    (64, 8, 1, 512, 4096, "Qwen2.5-72B at TP 8"),
+    (32, 28, 4, 256, 4096, "Qwen2.5-7B (group 7)"),
+]
+
+
+def run_decode_shapes(args):
+    """Paged decode alone across the head/batch shapes of configs 2-5.
+
+    Per shape: seeded contexts, random non-contiguous page tables, as many
+    distinct layer pools as fit in ~6 GB (so back-to-back launches never hit
+    in L2), decode launches back to back through the C ABI, CUDA events around
+    the loop. Prints one JSON line per shape (bytes = K/V of all contexts).
+    """
+    import torch
+    from mi_b200 import capi
+
+    dev = torch.device("cuda", dist_env()[2])
+    torch.cuda.set_device(dev)
+    lib = capi.lib()
+    ps, d = 16, 128
+    ws = torch.zeros(256 << 20, dtype=torch.uint8, device=dev)
+    st = torch.zeros(1, dtype=torch.int32, device=dev)
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    peak, _ = read_peak()
+    for (b, hq, hkv, lo, hi, note) in DECODE_SHAPES:
+        lens = np.random.default_rng(0).integers(lo, hi + 1, b).tolist()
+        P = sum(math.ceil(n / ps) for n in lens) + 16
+        L = max(2, min(16, int(6e9 // (P * 2 * ps * hkv * d * 2))))
+        pools = [torch.empty(P, 2, ps, hkv, d, device=dev, dtype=torch.bfloat16).normal_()
+                 for _ in range(L)]
+        perm = np.random.default_rng(1).permutation(P - 1)
+        indptr, indices, last, k0 = [0], [], [], 0
+        for n in lens:
+            k = math.ceil(n / ps)
+            indices += perm[k0:k0 + k].tolist()
+            k0 += k
+            indptr.append(len(indices))
+            last.append(n % ps or ps)
+        i32 = lambda x: torch.tensor(x, dtype=torch.int32, device=dev)  # noqa: E731
+        ip, ind, lp = i32(indptr), i32(indices), i32(last)
+        q = torch.randn(b, hq, d, device=dev, dtype=torch.bfloat16)
+        out = torch.empty_like(q)
+
+        def dec(pool):
+            return lib.mi_paged_decode(
+                q.data_ptr(), q.stride(0), q.stride(1), pool.data_ptr(), P, ps, hkv, d,
+                capi.DTYPE_BF16, ip.data_ptr(), ind.data_ptr(), lp.data_ptr(), b, hq,
+                1 / math.sqrt(d), out.data_ptr(), None, ws.data_ptr(), ws.numel(),
+                st.data_ptr(), stream)
+        rc = 0
+        for i in range(max(args.warmup, 3) * L):
+            rc |= dec(pools[i % L])
+        torch.cuda.synchronize()
+        reps = max(2, 200 // L)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            for pool in pools:
+                rc |= dec(pool)
+        e1.record()
+        torch.cuda.synchronize()
+        if rc or int(st.item()):
+            raise capi.MiError(f"decode failed: rc={rc} status={int(st.item())}")
+        us = e0.elapsed_time(e1) * 1e3 / (reps * L)
+        byt = sum(lens) * hkv * d * 2 * 2
+        print(json.dumps({"batch": b, "q_heads": hq, "kv_heads": hkv, "ctx": f"U[{lo},{hi}]",
+                          "mb_per_launch": round(byt / 1e6, 1), "us_per_launch": round(us, 2),
+                          "gbs": round(byt / us / 1e3, 1), "frac": round(byt / us / 1e3 / peak, 4),
+                          "layer_pools": L, "note": note}), flush=True)
+        del pools
+        torch.cuda.empty_cache()
+
+
+def prefill_flops(lens, hq=32, d=128) -> int:
+    """Causal prefill attention flops: sum_r 4*Hq*D*L_r(L_r+1)/2 (QK^T + PV)."""
+    return sum(4 * hq * d * n * (n + 1) // 2 for n in lens)
+
+
+def run_prefill(args):
+    """Kernel 3 on its own: ragged causal paged prefill of config 3's prompts.
+
+    32 requests, prompts U[128, 1024] (seeded), Mistral-7B attention shape
+    (32 Q / 8 KV heads, head_dim 128), bf16, page_size 16, random
+    non-contiguous page tables, K/V already in the pages (as after the append
+    of the same step). One launch per layer, each layer with its own pool;
+    ``--steps`` passes over ``--layers`` pools back to back, CUDA events
+    around the whole loop. Reports tensor TFLOP/s against the measured dense
+    bf16 peak (the burst figure: the kernel is timed alone).
+    """
+    import torch
+    from mi_b200 import capi
+    from mi_b200.prefill import BatchPrefillWithPagedKVCacheWrapper
+
+    rank, world, local = dist_env()
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    hq, hkv, d, ps = 32, 8, 128, 16
+    L = min(args.layers, 8)
+    rng = np.random.default_rng(3)
+    lens = rng.integers(128, 1025, 32).tolist()
+    npages = [math.ceil(n / ps) for n in lens]
+    P = sum(npages) + 1
+    perm = np.random.default_rng(4).permutation(P - 1)
+    indptr, indices, last, qo, k0 = [0], [], [], [0], 0
+    for n, k in zip(lens, npages):
+        indices.extend(perm[k0:k0 + k].tolist())
+        k0 += k
+        indptr.append(len(indices))
+        last.append(n % ps or ps)
+        qo.append(qo[-1] + n)
+    i32 = lambda x: torch.tensor(x, dtype=torch.int32, device=dev)  # noqa: E731
+    ip, ind, lp, qo_t = i32(indptr), i32(indices), i32(last), i32(qo)
+    g = torch.Generator(device=dev).manual_seed(7)
+    pools = [torch.randn(P, 2, ps, hkv, d, device=dev, dtype=torch.bfloat16, generator=g)
+             for _ in range(L)]
+    q = torch.randn(qo[-1], hq, d, device=dev, dtype=torch.bfloat16, generator=g)
+    out = torch.empty_like(q)
+    ws = torch.zeros(64 << 20, dtype=torch.uint8, device=dev)
+    w = BatchPrefillWithPagedKVCacheWrapper(ws)
+    w.plan(qo_t, ip, ind, lp, hq, hkv, d, ps, causal=True, q_data_type=torch.bfloat16)
+    for i in range(max(args.warmup, 3)):
+        for pool in pools:
+            w.run(q, pool, out=out)
+    torch.cuda.synchronize()
+    w.check_status()
+    K = max(1, min(args.steps, 20))
+    clocks = ClockSampler(local)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(K):
+        for pool in pools:
+            w.run(q, pool, out=out)
+    e1.record()
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    w.check_status()
+    ms = e0.elapsed_time(e1) / (K * L)
+    fl = prefill_flops(lens, hq, d)
+    tflops = fl / (ms / 1e3) / 1e12
+    peak = None
+    try:
+        with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as f:
+            peak = float(json.load(f)["bf16_tflops"])
+        kind = "measured"
+    except (OSError, KeyError, ValueError):
+        peak, kind = 1590.0, "fallback"
+    line = {"metric": "paged prefill attention TFLOP/s (config-3 prompts)",
+            "value": round(tflops, 1), "unit": "TFLOP/s", "n_gpus": 1, "steps": K,
+            "warmup": max(args.warmup, 3), "ms_per_step": round(ms, 4),
+            "higher_is_better": True, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "ragged causal paged prefill, 32 requests, prompts "
+                                   "U[128,1024] seeded, 32 Q / 8 KV heads, head_dim 128, "
+                                   "page_size 16", "tokens": qo[-1], "layers_pools": L},
+            "roofline": {"bound": "tensor", "kernel": "prefill_tc_kernel",
+                         "achieved": round(tflops, 1), "peak": peak, "unit": "TFLOP/s",
+                         "frac": round(tflops / peak, 4), "peak_kind": kind,
+                         "algorithmic_flops": fl, "avg_launch_us": round(ms * 1e3, 2)},
+            "clocks": clk, "gpu_launches": K * L}
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------
 def parse_args():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -342,8 +510,10 @@ def parse_args():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-model", action="store_true",
                     help="skip the Mistral-7B-shape decode measurement (config 3)")
-    ap.add_argument("--workload", choices=["config2", "config5"], default="config2",
-                    help="config5: Qwen2.5-72B tensor-parallel decode over the launch's GPUs")
+    ap.add_argument("--workload", choices=["config2", "config5", "prefill", "decode-shapes"],
+                    default="config2",
+                    help="config5: Qwen2.5-72B tensor-parallel decode over the launch's GPUs; "
+                         "prefill: the paged prefill kernel alone on config 3's prompts")
     ap.add_argument("--model", default=None, help="config5: model preset (default qwen2.5-72b)")
     ap.add_argument("--batch", type=int, default=None, help="config5: requests (default 64)")
     ap.add_argument("--decode-steps", type=int, default=None,
@@ -402,6 +572,12 @@ def main():
         return
     if args.workload == "config5":
         run_tp_decode(args)
+        return
+    if args.workload == "prefill":
+        run_prefill(args)
+        return
+    if args.workload == "decode-shapes":
+        run_decode_shapes(args)
         return
     import torch
     import torch.distributed as dist
