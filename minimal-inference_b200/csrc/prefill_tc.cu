@@ -13,7 +13,9 @@
 //   warp 1  MMA issuer (one thread): S = Q K^T into TMEM (M=128, N=128,
 //           K=head_dim, both operands K-major), then O += P V into TMEM
 //           (P K-major from shared memory, V MN-major), tcgen05.commit to
-//           mbarriers;
+//           mbarriers. S of tile j+1 is issued as soon as the softmax warps
+//           hold S of tile j in registers, so it runs under their softmax;
+//           P V of tile j follows once P is written;
 //   warps 2-5  softmax and epilogue: thread = TMEM lane = query row. Each KV
 //           tile: load the S row, causal/length mask, online softmax in the
 //           exp2 domain, write the bf16 P row into a 128-byte-swizzled tile,
@@ -229,13 +231,6 @@ __global__ void __launch_bounds__(kThreadsP, 1)
     mbar_init(p_full, 4);
     mbar_init(o_done, 1);
   }
-  {  // V rows past a request's end are multiplied by P = 0: keep them finite
-    uint4 z = make_uint4(0, 0, 0, 0);
-    for (int st = 0; st < 2; ++st) {
-      uint4 *v = reinterpret_cast<uint4 *>(smem + L::KV_OFF + st * L::STAGE_BYTES + L::K_BYTES);
-      for (int i = threadIdx.x; i < L::V_BYTES / 16; i += blockDim.x) v[i] = z;
-    }
-  }
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                      smem_u32(tmem_slot)),
@@ -275,6 +270,18 @@ __global__ void __launch_bounds__(kThreadsP, 1)
         break;
       }
       const int nvc = min(8, cdiv(lk - tok_tile, 16));
+      if (j < 2 && nvc < 8) {
+        // V chunks past the request's end are multiplied by P = 0; on a
+        // stage's first use they hold whatever shared memory held, so zero
+        // them (later uses keep the previous tile's finite values there)
+        for (int dh = 0; dh < DH; ++dh) {
+          uint4 *v = reinterpret_cast<uint4 *>(smem + L::KV_OFF + s * L::STAGE_BYTES +
+                                               L::K_BYTES + dh * (kN * 128) + nvc * 16 * 128);
+          for (int i = lane; i < (8 - nvc) * 16 * 128 / 16; i += 32) v[i] = make_uint4(0, 0, 0, 0);
+        }
+        fence_proxy_async_smem();  // the zeros are visible to the tensor core
+        __syncwarp();
+      }
       if (lane == 0) mbar_arrive_expect_tx(&kv_full[s], nvc * 2 * DH * 2048);
       __syncwarp();
       const int c = min(lane / (2 * DH), 7), which = (lane / DH) & 1, dh = lane % DH;
@@ -304,14 +311,9 @@ __global__ void __launch_bounds__(kThreadsP, 1)
       const uint32_t idesc_pv = umma_idesc(fmt, true, D, kM);
       const uint32_t q_addr = smem_u32(smem + L::Q_OFF);
       const uint32_t p_addr = smem_u32(smem + L::P_OFF);
-      if (!mbar_wait_bounded(q_full, 0)) ok = false;
-      for (int j = 0; j < n_tiles && ok; ++j) {
-        const int s = j & 1;
-        const uint32_t k_addr = smem_u32(smem + L::KV_OFF + s * L::STAGE_BYTES);
-        const uint32_t v_addr = k_addr + L::K_BYTES;
-        if (!mbar_wait_bounded(&kv_full[s], (j >> 1) & 1)) { ok = false; break; }
-        if (j > 0 && !mbar_wait_bounded(s_free, (j - 1) & 1)) { ok = false; break; }
-        tc_fence_after();
+      // S = Q K_j^T for the K tile in stage j & 1
+      auto issue_qk = [&](int j) {
+        const uint32_t k_addr = smem_u32(smem + L::KV_OFF + (j & 1) * L::STAGE_BYTES);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t off = (kk >> 2) * (kM * 128) + (kk & 3) * 32;
@@ -320,6 +322,24 @@ __global__ void __launch_bounds__(kThreadsP, 1)
                idesc_qk, kk > 0);
         }
         umma_commit(s_full);
+      };
+      if (!mbar_wait_bounded(q_full, 0) || !mbar_wait_bounded(&kv_full[0], 0)) ok = false;
+      if (ok) {
+        tc_fence_after();
+        issue_qk(0);
+      }
+      for (int j = 0; j < n_tiles && ok; ++j) {
+        const int s = j & 1;
+        const uint32_t v_addr = smem_u32(smem + L::KV_OFF + s * L::STAGE_BYTES) + L::K_BYTES;
+        if (j + 1 < n_tiles) {  // S_{j+1} once S_j is out of TMEM, under softmax j
+          if (!mbar_wait_bounded(s_free, j & 1) ||
+              !mbar_wait_bounded(&kv_full[(j + 1) & 1], ((j + 1) >> 1) & 1)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          issue_qk(j + 1);
+        }
         if (!mbar_wait_bounded(p_full, j & 1)) { ok = false; break; }
         tc_fence_after();
 #pragma unroll
