@@ -169,8 +169,13 @@ int mi_paged_decode_noalloc(
  * attending to each request's pages (appended first). With causal != 0,
  * query i of a request with qo_len queries and kv_len keys sees keys
  * j <= kv_len - qo_len + i. out: contiguous [total_q][num_qo_heads][head_dim];
- * lse optional as for decode. The workspace is reserved for split-K of long
- * requests; pass mi_paged_prefill_workspace_size() bytes (may be 0).
+ * lse optional as for decode. The workspace (mi_paged_prefill_workspace_size()
+ * bytes, 16-byte aligned) holds the work-item counters the persistent
+ * tensor-core kernel shares between its CTAs: zero-fill it once before its
+ * first use; every call leaves it at zero again (after MI_STATUS_TIMEOUT,
+ * zero-fill it again), and calls sharing a workspace must not overlap on the
+ * GPU. Without a workspace (NULL or smaller) the kernel assigns work items
+ * round robin instead.
  * ------------------------------------------------------------------------- */
 size_t mi_paged_prefill_workspace_size(int32_t total_q, int32_t batch_size,
                                        int32_t num_qo_heads, int32_t head_dim);

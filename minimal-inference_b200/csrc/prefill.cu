@@ -106,7 +106,7 @@ extern "C" size_t mi_paged_prefill_workspace_size(int32_t total_q, int32_t batch
   (void)batch_size;
   (void)num_qo_heads;
   (void)head_dim;
-  return 0;
+  return 256;  // the tensor-core kernel's two work-item counters
 }
 
 extern "C" int mi_paged_prefill(
@@ -119,8 +119,6 @@ extern "C" int mi_paged_prefill(
     void *out, float *lse, void *workspace, size_t workspace_bytes, int32_t *status,
     mi_stream_t stream) {
   using namespace mi;
-  (void)workspace;
-  (void)workspace_bytes;
   MI_REQUIRE(total_q >= 0 && batch_size >= 0, "prefill: negative total_q/batch_size");
   if (total_q == 0 || batch_size == 0) return MI_OK;
   MI_REQUIRE(q && qo_indptr && kv_data && kv_indptr && kv_indices && kv_last_page_len && out,
@@ -137,7 +135,11 @@ extern "C" int mi_paged_prefill(
   PrefillParams p{q, q_stride_n, q_stride_h, qo_indptr, total_q, kv_data, num_pages, page_size,
                   num_kv_heads, head_dim, kv_indptr, kv_indices, kv_last_page_len, batch_size,
                   num_qo_heads, num_qo_heads / num_kv_heads, causal != 0, sm_scale * kLog2e,
-                  out, lse, status};
+                  out, lse, status, nullptr};
+  // work-item counters for the persistent tensor-core kernel (without a
+  // workspace it falls back to a fixed round robin)
+  if (workspace && workspace_bytes >= 256 && (reinterpret_cast<uintptr_t>(workspace) & 15) == 0)
+    p.ctr = static_cast<unsigned *>(workspace);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const int rc = launch_prefill_tc(p, dtype, s);
   if (rc >= 0) return rc;

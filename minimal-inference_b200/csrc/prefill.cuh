@@ -20,6 +20,7 @@ struct PrefillParams {
   void *out;
   float *lse;
   int32_t *status;
+  unsigned *ctr;  // [2] work-item counters in the workspace (zero between calls), or null
 };
 
 // Tensor-core path (prefill_tc.cu). Returns -1 (nothing launched) when the

@@ -4,9 +4,13 @@
 // scheduler.py:530-534, :704-716, model.py:235) for bf16/fp16, head_dim
 // 64/128, page_size a multiple of 16.
 //
-// CTA = (request, KV head, 128 "packed" query rows): a row is a (query token,
-// query head of the GQA group) pair, row = token * group + head, so one K/V
-// tile feeds the whole group (Tq = 128 / group tokens per CTA). Six warps:
+// Work item = (request, KV head, 128 "packed" query rows): a row is a (query
+// token, query head of the GQA group) pair, row = token * group + head, so one
+// K/V tile feeds the whole group (Tq = 128 / group tokens per item). The grid
+// is persistent, one CTA per SM; CTAs take items from a counter shared
+// through the workspace (each request's heaviest query tiles first), so set-up
+// (barriers, TMEM, the query-tile prefix) is paid once per SM and the next
+// item's metadata, Q and K/V loads run under the current item. Six warps:
 //   warp 0  producer: TMA loads of the Q tile (3-D map over q) and of 128-token
 //           K/V tiles straight from the pages (4-D pool map, 16-token boxes),
 //           two K/V stages, 128-byte swizzle;
@@ -19,10 +23,12 @@
 //   warps 2-5  softmax and epilogue: thread = TMEM lane = query row. Each KV
 //           tile: load the S row, causal/length mask, online softmax in the
 //           exp2 domain, write the bf16 P row into a 128-byte-swizzled tile,
-//           rescale the O row in TMEM when the row max moved; at the end
-//           normalise O and store it.
-// TMEM: S in columns [0,128), O in [128, 128+head_dim). Every wait is
-// bounded; TMEM is freed on every path.
+//           rescale the O row in TMEM only when the row max grew by more
+//           than 2^8; at the end normalise O and store it.
+// TMEM: S in columns [0,128), two O buffers (items alternate, so one item's
+// first products go in while the previous item's epilogue reads). Every wait
+// is bounded; TMEM is freed on every path.
+#include <algorithm>
 #include <type_traits>
 
 #include "prefill.cuh"
@@ -46,9 +52,13 @@ template <int D> struct PfLayout {
   static constexpr int Q_OFF = 0;
   static constexpr int KV_OFF = Q_OFF + Q_BYTES;
   static constexpr int P_OFF = KV_OFF + 2 * STAGE_BYTES;
-  static constexpr int BAR_OFF = P_OFF + P_BYTES;      // 10 mbarriers + tmem base
-  static constexpr int META_OFF = BAR_OFF + 128;
+  static constexpr int BAR_OFF = P_OFF + P_BYTES;      // 18 mbarriers + tmem base
+  static constexpr int ITEM_OFF = BAR_OFF + 256;       // 2 work-item records
+  static constexpr int META_OFF = ITEM_OFF + 64;
   static constexpr int SMEM = META_OFF + (kMaxBatchTc + 1) * 4 + 1024;
+  // TMEM: S in [0, 128), O buffers at 128 and 128 + OB_STRIDE (head_dim wide)
+  static constexpr int OB_STRIDE = D;
+  static constexpr int TMEM_COLS = kN + 2 * D <= 256 ? 256 : 512;
 };
 
 // UMMA shared-memory descriptor, 128-byte swizzle (sm100 layout): start >> 4
@@ -127,6 +137,20 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float *v) {
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
+// 2^x with the hardware approximation (PTX ex2.approx, relative error below
+// 2^-22, 2^-inf = 0): P is rounded to 16 bits right after, so the accurate
+// library path would buy nothing here.
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// A row's running max moves only when a tile's max exceeds it by more than
+// this (log2 units): until then P = 2^(s - m) stays below 2^8, exact enough
+// in bf16/fp16 and far from overflow in the fp32 sums, and O needs no rescale.
+constexpr float kRescaleLog2 = 8.f;
+
 template <typename T> struct Pack2;
 template <> struct Pack2<__nv_bfloat16> {
   __device__ __forceinline__ static uint32_t run(float a, float b) {
@@ -141,6 +165,13 @@ template <> struct Pack2<__half> {
   }
 };
 
+// One work item = (request b, KV head h, query tile t0): the item record the
+// producer hands to the MMA and softmax warps through a two-slot ring.
+struct __align__(16) PfItem {
+  int b, h, t0, n_tiles;  // b < 0: no more items
+  int q_start, lq, lk, page_base;
+};
+
 template <typename T, int D>
 __global__ void __launch_bounds__(kThreadsP, 1)
     prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap,
@@ -151,19 +182,19 @@ __global__ void __launch_bounds__(kThreadsP, 1)
   unsigned char *smem = reinterpret_cast<unsigned char *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L::BAR_OFF);
-  uint64_t *q_full = bars + 0, *kv_full = bars + 1, *kv_empty = bars + 3;
-  uint64_t *s_full = bars + 5, *s_free = bars + 6, *p_full = bars + 7, *o_done = bars + 8;
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 10);
+  uint64_t *q_full = bars + 0, *q_empty = bars + 1, *kv_full = bars + 2, *kv_empty = bars + 4;
+  uint64_t *s_full = bars + 6, *s_free = bars + 7, *p_full = bars + 8, *o_done = bars + 9;
+  uint64_t *o_full = bars + 10, *o_free = bars + 12, *it_full = bars + 14, *it_empty = bars + 16;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 18);
+  PfItem *items = reinterpret_cast<PfItem *>(smem + L::ITEM_OFF);
   int *tiles_pre = reinterpret_cast<int *>(smem + L::META_OFF);
-  __shared__ int s_info[2];
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int h = blockIdx.y;
   const int g = p.group;
-  const int tq = kM / g;        // query tokens per CTA
+  const int tq = kM / g;        // query tokens per item
   const int m_used = tq * g;    // packed rows in use
 
-  // ---- which request / query tile is this CTA ------------------------------
+  // ---- once per CTA: query-tile prefix over requests, barriers, TMEM ------
   if (warp == 0) {  // tiles_pre[i] = sum over b < i of ceil(qo_len_b / tq)
     int carry = 0;
     if (lane == 0) tiles_pre[0] = 0;
@@ -178,131 +209,138 @@ __global__ void __launch_bounds__(kThreadsP, 1)
       if (bb < p.batch) tiles_pre[bb + 1] = carry + x;
       carry += __shfl_sync(0xffffffffu, x, 31);
     }
-  }
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    const int tile = blockIdx.x;
-    int b = -1;
-    if (tile < tiles_pre[p.batch]) {
-      int lo = 0, hi = p.batch - 1;
-      while (lo < hi) {
-        const int mid = (lo + hi + 1) >> 1;
-        if (tiles_pre[mid] <= tile) lo = mid; else hi = mid - 1;
+  } else if (warp == 1) {
+    if (lane == 0) {
+      mbar_init(q_full, 1);
+      mbar_init(q_empty, 1);
+      for (int i = 0; i < 2; ++i) {
+        mbar_init(&kv_full[i], 1);
+        mbar_init(&kv_empty[i], 1);
+        mbar_init(&o_full[i], 1);
+        mbar_init(&o_free[i], 4);
+        mbar_init(&it_full[i], 1);
+        mbar_init(&it_empty[i], 5);  // the MMA thread and the 4 softmax warps
       }
-      b = lo;
+      mbar_init(s_full, 1);
+      mbar_init(s_free, 4);
+      mbar_init(p_full, 4);
+      mbar_init(o_done, 1);
     }
-    s_info[0] = b;
-    s_info[1] = b >= 0 ? (tile - tiles_pre[b]) * tq : 0;
-  }
-  __syncthreads();
-  const int b = s_info[0];
-  if (b < 0) return;  // past the last query tile
-  const int t0 = s_info[1];
-  const int q_start = p.qo_indptr[b];
-  const int lq = p.qo_indptr[b + 1] - q_start;
-  const int lk = kv_len_of(p.indptr, p.last, b, p.ps);
-  const int rows_tok = min(tq, lq - t0);
-  int lim_tok = p.causal ? min(lk, lk - lq + t0 + rows_tok) : lk;
-  const int n_tiles = lim_tok > 0 ? cdiv(lim_tok, kN) : 0;
-
-  if (n_tiles == 0) {  // no visible key: zeros, lse = -inf (warps 2..5)
-    if (warp >= 2) {
-      const int r = (warp & 3) * 32 + lane;
-      const int t = r / g, j = r % g;
-      if (r < m_used && t < rows_tok) {
-        T *o = static_cast<T *>(p.out) +
-               (static_cast<int64_t>(q_start + t0 + t) * p.hq + h * g + j) * D;
-        for (int i = 0; i < D; ++i) o[i] = Elt<T>::from(0.f);
-        if (p.lse) p.lse[static_cast<int64_t>(q_start + t0 + t) * p.hq + h * g + j] = -INFINITY;
-      }
-    }
-    return;
-  }
-
-  // ---- setup: barriers, zeroed V stages, TMEM ------------------------------
-  if (threadIdx.x == 0) {
-    mbar_init(q_full, 1);
-    mbar_init(&kv_full[0], 1);
-    mbar_init(&kv_full[1], 1);
-    mbar_init(&kv_empty[0], 1);
-    mbar_init(&kv_empty[1], 1);
-    mbar_init(s_full, 1);
-    mbar_init(s_free, 4);
-    mbar_init(p_full, 4);
-    mbar_init(o_done, 1);
-  }
-  if (warp == 1) {
+    __syncwarp();
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                      smem_u32(tmem_slot)),
-                 "r"(256)
+                 "r"(L::TMEM_COLS)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
   fence_mbar_init();
-  fence_proxy_async_smem();
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t tmem_s = tmem, tmem_o = tmem + kN;
+  const uint32_t tmem_s = tmem;  // S: columns [0, 128); O buffers at 128 and 128 + kObStride
+  const int n_items = tiles_pre[p.batch] * p.hkv;
   bool ok = true;
 
   if (warp == 0) {
     // ============================ producer ==================================
     const uint64_t pol_q = evict_last_policy(), pol_kv = evict_first_policy();
-    if (lane == 0) {
-      mbar_arrive_expect_tx(q_full, DH * m_used * 128);
-      for (int dh = 0; dh < DH; ++dh)
-        tma_load_3d(smem + L::Q_OFF + dh * kM * 128, &qmap, dh * 64, h * g, q_start + t0, q_full,
-                    pol_q);
-    }
-    const int page_base = p.indptr[b];
-    const int nbox = 8 * 2 * DH;  // (16-token chunk, K/V, d block)
-    for (int j = 0; j < n_tiles && ok; ++j) {
-      const int s = j & 1;
-      const int tok_tile = j * kN;
-      // page id of chunk c = lane (c < 8)
-      const int tok_c = tok_tile + lane * 16;
-      int pg = -1;
-      if (lane < 8 && tok_c < lk) pg = p.indices[page_base + tok_c / p.ps];
-      if (!__all_sync(0xffffffffu, mbar_wait_bounded(&kv_empty[s], ((j >> 1) & 1) ^ 1))) {
+    int gt = 0, qc = 0;
+    for (int it = 0; ok; ++it) {
+      // next item: a counter shared by all CTAs (heaviest query tiles of each
+      // request first), or round robin without a workspace
+      int k = 0;
+      if (lane == 0) k = p.ctr ? static_cast<int>(atomicAdd(p.ctr, 1u)) : blockIdx.x + it * gridDim.x;
+      k = __shfl_sync(0xffffffffu, k, 0);
+      PfItem rec{-1, 0, 0, 0, 0, 0, 0, 0};
+      if (k < n_items) {
+        int lo = 0, hi = p.batch - 1;  // last b with tiles_pre[b] * hkv <= k
+        while (lo < hi) {
+          const int mid = (lo + hi + 1) >> 1;
+          if (tiles_pre[mid] * p.hkv <= k) lo = mid; else hi = mid - 1;
+        }
+        const int b = lo, ntq = tiles_pre[b + 1] - tiles_pre[b];
+        const int rem = k - tiles_pre[b] * p.hkv;
+        rec.b = b;
+        rec.h = rem / ntq;
+        rec.t0 = (ntq - 1 - rem % ntq) * tq;
+        rec.q_start = p.qo_indptr[b];
+        rec.lq = p.qo_indptr[b + 1] - rec.q_start;
+        rec.lk = kv_len_of(p.indptr, p.last, b, p.ps);
+        rec.page_base = p.indptr[b];
+        const int rows_tok = min(tq, rec.lq - rec.t0);
+        const int lim_tok =
+            p.causal ? min(rec.lk, rec.lk - rec.lq + rec.t0 + rows_tok) : rec.lk;
+        rec.n_tiles = lim_tok > 0 ? cdiv(lim_tok, kN) : 0;
+      }
+      const int slot = it & 1;
+      if (it >= 2 && !__all_sync(0xffffffffu, mbar_wait_bounded(&it_empty[slot], ((it >> 1) - 1) & 1))) {
         ok = false;
         break;
       }
-      const int nvc = min(8, cdiv(lk - tok_tile, 16));
-      if (j < 2 && nvc < 8) {
-        // V chunks past the request's end are multiplied by P = 0; on a
-        // stage's first use they hold whatever shared memory held, so zero
-        // them (later uses keep the previous tile's finite values there)
-        for (int dh = 0; dh < DH; ++dh) {
-          uint4 *v = reinterpret_cast<uint4 *>(smem + L::KV_OFF + s * L::STAGE_BYTES +
-                                               L::K_BYTES + dh * (kN * 128) + nvc * 16 * 128);
-          for (int i = lane; i < (8 - nvc) * 16 * 128 / 16; i += 32) v[i] = make_uint4(0, 0, 0, 0);
-        }
-        fence_proxy_async_smem();  // the zeros are visible to the tensor core
-        __syncwarp();
+      if (lane == 0) {
+        items[slot] = rec;
+        mbar_arrive(&it_full[slot]);
       }
-      if (lane == 0) mbar_arrive_expect_tx(&kv_full[s], nvc * 2 * DH * 2048);
-      __syncwarp();
-      const int c = min(lane / (2 * DH), 7), which = (lane / DH) & 1, dh = lane % DH;
-      const int page = __shfl_sync(0xffffffffu, pg, c);
-      if (lane < nbox) {
-        if (c < nvc) {
+      if (rec.b < 0) break;
+      if (rec.n_tiles == 0) continue;
+      // Q tile into the single Q buffer once the previous item's last QK^T is done
+      if (qc > 0 && !__all_sync(0xffffffffu, mbar_wait_bounded(q_empty, (qc - 1) & 1))) {
+        ok = false;
+        break;
+      }
+      if (lane == 0) {
+        mbar_arrive_expect_tx(q_full, DH * m_used * 128);
+        for (int dh = 0; dh < DH; ++dh)
+          tma_load_3d(smem + L::Q_OFF + dh * kM * 128, &qmap, dh * 64, rec.h * g,
+                      rec.q_start + rec.t0, q_full, pol_q);
+      }
+      ++qc;
+      const int nbox = 8 * 2 * DH;  // (16-token chunk, K/V, d block)
+      for (int j = 0; j < rec.n_tiles; ++j, ++gt) {
+        const int s = gt & 1;
+        const int tok_tile = j * kN;
+        const int tok_c = tok_tile + lane * 16;  // page id of chunk c = lane (c < 8)
+        int pg = -1;
+        if (lane < 8 && tok_c < rec.lk) pg = p.indices[rec.page_base + tok_c / p.ps];
+        if (gt >= 2 && !__all_sync(0xffffffffu, mbar_wait_bounded(&kv_empty[s], ((gt >> 1) - 1) & 1))) {
+          ok = false;
+          break;
+        }
+        const int nvc = min(8, cdiv(rec.lk - tok_tile, 16));
+        if (gt < 2 && nvc < 8) {
+          // V chunks past the request's end are multiplied by P = 0; on a
+          // stage's first use they hold whatever shared memory held, so zero
+          // them (later uses keep an earlier tile's finite values there)
+          for (int dh = 0; dh < DH; ++dh) {
+            uint4 *v = reinterpret_cast<uint4 *>(smem + L::KV_OFF + s * L::STAGE_BYTES +
+                                                 L::K_BYTES + dh * (kN * 128) + nvc * 16 * 128);
+            for (int i = lane; i < (8 - nvc) * 16 * 128 / 16; i += 32) v[i] = make_uint4(0, 0, 0, 0);
+          }
+          fence_proxy_async_smem();  // the zeros are visible to the tensor core
+          __syncwarp();
+        }
+        if (lane == 0) mbar_arrive_expect_tx(&kv_full[s], nvc * 2 * DH * 2048);
+        __syncwarp();
+        const int c = min(lane / (2 * DH), 7), which = (lane / DH) & 1, dh = lane % DH;
+        const int page = __shfl_sync(0xffffffffu, pg, c);
+        if (lane < nbox && c < nvc) {
           const int tok = tok_tile + c * 16;
           const bool bad = page < 0 || page >= p.num_pages;
           unsigned char *dst = smem + L::KV_OFF + s * L::STAGE_BYTES + which * L::K_BYTES +
                                dh * (kN * 128) + c * 16 * 128;
           // a bad page id loads from page 0 (in bounds) and is flagged; its
           // keys still count, so the result is wrong but nothing faults
-          tma_load_4d(dst, &kvmap, dh * 64, h, tok % p.ps, (bad ? 0 : page) * 2 + which,
+          tma_load_4d(dst, &kvmap, dh * 64, rec.h, tok % p.ps, (bad ? 0 : page) * 2 + which,
                       &kv_full[s], pol_kv);
           if (bad && which == 0 && dh == 0) flag(p.status, MI_STATUS_BAD_PAGE);
         }
       }
     }
     // no copy may be in flight when the CTA retires
-    for (int j = max(0, n_tiles - 2); j < n_tiles; ++j)
-      if (!__all_sync(0xffffffffu, mbar_wait_bounded(&kv_full[j & 1], (j >> 1) & 1))) ok = false;
+    if (qc > 0 && !__all_sync(0xffffffffu, mbar_wait_bounded(q_full, (qc - 1) & 1))) ok = false;
+    for (int t = max(0, gt - 2); t < gt; ++t)
+      if (!__all_sync(0xffffffffu, mbar_wait_bounded(&kv_full[t & 1], (t >> 1) & 1))) ok = false;
   } else if (warp == 1) {
     // ============================ MMA issuer ================================
     if (lane == 0) {
@@ -311,9 +349,8 @@ __global__ void __launch_bounds__(kThreadsP, 1)
       const uint32_t idesc_pv = umma_idesc(fmt, true, D, kM);
       const uint32_t q_addr = smem_u32(smem + L::Q_OFF);
       const uint32_t p_addr = smem_u32(smem + L::P_OFF);
-      // S = Q K_j^T for the K tile in stage j & 1
-      auto issue_qk = [&](int j) {
-        const uint32_t k_addr = smem_u32(smem + L::KV_OFF + (j & 1) * L::STAGE_BYTES);
+      auto issue_qk = [&](int t) {  // S = Q K^T of global tile t (stage t & 1)
+        const uint32_t k_addr = smem_u32(smem + L::KV_OFF + (t & 1) * L::STAGE_BYTES);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t off = (kk >> 2) * (kM * 128) + (kk & 3) * 32;
@@ -323,37 +360,82 @@ __global__ void __launch_bounds__(kThreadsP, 1)
         }
         umma_commit(s_full);
       };
-      if (!mbar_wait_bounded(q_full, 0) || !mbar_wait_bounded(&kv_full[0], 0)) ok = false;
-      if (ok) {
-        tc_fence_after();
-        issue_qk(0);
+      // Items come in order; the next item with keys is looked up ahead so
+      // its first QK^T can run under the softmax of this item's last tile.
+      int it = 0, gt = 0, qc = 0, oc = 0;
+      auto next_item = [&](PfItem &r) -> bool {  // the next record with keys; false at the end
+        for (;;) {
+          const int slot = it & 1;
+          if (!mbar_wait_bounded(&it_full[slot], (it >> 1) & 1)) { ok = false; return false; }
+          r = items[slot];
+          mbar_arrive(&it_empty[slot]);  // the record is copied
+          ++it;
+          if (r.b < 0) return false;
+          if (r.n_tiles > 0) return true;
+        }
+      };
+      PfItem cur, nxt;
+      bool have = next_item(cur), have_next = false;
+      if (have) {  // first QK^T
+        if (!mbar_wait_bounded(q_full, 0) || !mbar_wait_bounded(&kv_full[0], 0)) ok = false;
+        if (ok) {
+          tc_fence_after();
+          issue_qk(0);
+          if (cur.n_tiles == 1) umma_commit(q_empty);
+        }
       }
-      for (int j = 0; j < n_tiles && ok; ++j) {
-        const int s = j & 1;
-        const uint32_t v_addr = smem_u32(smem + L::KV_OFF + s * L::STAGE_BYTES) + L::K_BYTES;
-        if (j + 1 < n_tiles) {  // S_{j+1} once S_j is out of TMEM, under softmax j
-          if (!mbar_wait_bounded(s_free, j & 1) ||
-              !mbar_wait_bounded(&kv_full[(j + 1) & 1], ((j + 1) >> 1) & 1)) {
+      int last_gt = -1;
+      while (have && ok) {
+        const int ob = oc & 1;
+        const uint32_t tmem_o = tmem + kN + ob * L::OB_STRIDE;
+        for (int j = 0; j < cur.n_tiles && ok; ++j, ++gt) {
+          // look ahead: QK^T of the next tile (this item's, or the next item's first)
+          bool ahead = j + 1 < cur.n_tiles;
+          bool cross = false;
+          if (!ahead) {
+            have_next = next_item(nxt);
+            ahead = cross = have_next;
+          }
+          if (ahead) {
+            if (!mbar_wait_bounded(s_free, gt & 1) ||
+                (cross && !mbar_wait_bounded(q_full, (qc + 1) & 1)) ||
+                !mbar_wait_bounded(&kv_full[(gt + 1) & 1], ((gt + 1) >> 1) & 1)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            issue_qk(gt + 1);
+            // the last QK^T of its item frees the Q buffer for the item after
+            const bool last_qk = cross ? nxt.n_tiles == 1 : j + 2 == cur.n_tiles;
+            if (last_qk) umma_commit(q_empty);
+          }
+          if (!mbar_wait_bounded(p_full, gt & 1)) { ok = false; break; }
+          if (j == 0 && oc >= 2 && !mbar_wait_bounded(&o_free[ob], ((oc >> 1) - 1) & 1)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          issue_qk(j + 1);
-        }
-        if (!mbar_wait_bounded(p_full, j & 1)) { ok = false; break; }
-        tc_fence_after();
+          const uint32_t v_addr = smem_u32(smem + L::KV_OFF + (gt & 1) * L::STAGE_BYTES) + L::K_BYTES;
 #pragma unroll
-        for (int kk = 0; kk < kN / 16; ++kk) {
-          const uint32_t aoff = (kk >> 2) * (kM * 128) + (kk & 3) * 32;
-          // V: MN-major, 64-wide d blocks kN*128 bytes apart, 8-token groups 1 KB apart
-          umma(tmem_o, umma_desc(p_addr + aoff, 16, 1024),
-               umma_desc(v_addr + kk * 16 * 128, kN * 128, 1024), idesc_pv, (j > 0 || kk > 0));
+          for (int kk = 0; kk < kN / 16; ++kk) {
+            const uint32_t aoff = (kk >> 2) * (kM * 128) + (kk & 3) * 32;
+            // V: MN-major, 64-wide d blocks kN*128 bytes apart, 8-token groups 1 KB apart
+            umma(tmem_o, umma_desc(p_addr + aoff, 16, 1024),
+                 umma_desc(v_addr + kk * 16 * 128, kN * 128, 1024), idesc_pv, (j > 0 || kk > 0));
+          }
+          umma_commit(&kv_empty[gt & 1]);
+          umma_commit(o_done);
+          if (j + 1 == cur.n_tiles) umma_commit(&o_full[ob]);
+          last_gt = gt;
         }
-        umma_commit(&kv_empty[s]);
-        umma_commit(o_done);
+        ++qc;
+        ++oc;
+        have = have_next;
+        cur = nxt;
+        have_next = false;
       }
       // the last products must land before TMEM is freed
-      if (ok && !mbar_wait_bounded(o_done, (n_tiles - 1) & 1)) ok = false;
+      if (last_gt >= 0 && !mbar_wait_bounded(o_done, last_gt & 1)) ok = false;
     }
     __syncwarp();
   } else {
@@ -361,82 +443,109 @@ __global__ void __launch_bounds__(kThreadsP, 1)
     const int qd = warp & 3;
     const int r = qd * 32 + lane;  // packed row == TMEM lane
     const int t = r / g, jh = r % g;
-    const bool row_ok = r < m_used && t < rows_tok;
-    int lim = p.causal ? lk - lq + t0 + t + 1 : lk;
-    lim = min(lim, lk);
-    if (!row_ok) lim = 0;
     const uint32_t lane_base = static_cast<uint32_t>(qd * 32) << 16;
-    float m = -INFINITY, l = 0.f;
     unsigned char *prow = smem + L::P_OFF;
-    for (int j = 0; j < n_tiles; ++j) {
-      if (!__all_sync(0xffffffffu, mbar_wait_bounded(s_full, j & 1))) { ok = false; break; }
-      tc_fence_after();
-      float sv[kN];
-#pragma unroll
-      for (int c = 0; c < kN / 32; ++c) tmem_ld32(tmem_s + lane_base + c * 32, sv + c * 32);
-      tmem_wait_ld();
-      tc_fence_before();
+    int gt = 0, oc = 0;
+    for (int it = 0; ok; ++it) {
+      const int slot = it & 1;
+      if (!__all_sync(0xffffffffu, mbar_wait_bounded(&it_full[slot], (it >> 1) & 1))) {
+        ok = false;
+        break;
+      }
+      const PfItem rec = items[slot];
       __syncwarp();
-      if (lane == 0) mbar_arrive(s_free);
-      const int kbase = j * kN;
-      float mt = -INFINITY;
-#pragma unroll
-      for (int c = 0; c < kN; ++c) {
-        sv[c] = (kbase + c < lim) ? sv[c] * p.scale_log2 : -INFINITY;
-        mt = fmaxf(mt, sv[c]);
+      if (lane == 0) mbar_arrive(&it_empty[slot]);
+      if (rec.b < 0) break;
+      const int rows_tok = min(tq, rec.lq - rec.t0);
+      const bool row_ok = r < m_used && t < rows_tok;
+      const int64_t orow = static_cast<int64_t>(rec.q_start + rec.t0 + t) * p.hq + rec.h * g + jh;
+      if (rec.n_tiles == 0) {  // no visible key: zeros, lse = -inf
+        if (row_ok) {
+          T *o = static_cast<T *>(p.out) + orow * D;
+          for (int i = 0; i < D; ++i) o[i] = Elt<T>::from(0.f);
+          if (p.lse) p.lse[orow] = -INFINITY;
+        }
+        continue;
       }
-      const float m_new = fmaxf(m, mt);
-      const float ms = m_new == -INFINITY ? 0.f : m_new;
-      const float corr = m == m_new ? 1.f : exp2f(m - ms);
-      float sum = 0.f;
-#pragma unroll
-      for (int c = 0; c < kN; ++c) {
-        sv[c] = exp2f(sv[c] - ms);
-        sum += sv[c];
-      }
-      l = l * corr + sum;
-      m = m_new;
-      // P_{j-1} must have been consumed (and O_{j-1} complete) before P_j / O
-      if (j > 0) {
-        if (!__all_sync(0xffffffffu, mbar_wait_bounded(o_done, (j - 1) & 1))) { ok = false; break; }
+      int lim = p.causal ? rec.lk - rec.lq + rec.t0 + t + 1 : rec.lk;
+      lim = min(lim, rec.lk);
+      if (!row_ok) lim = 0;
+      const int ob = oc & 1;
+      const uint32_t tmem_o = tmem + kN + ob * L::OB_STRIDE;
+      float m = -INFINITY, l = 0.f;
+      for (int j = 0; j < rec.n_tiles; ++j, ++gt) {
+        if (!__all_sync(0xffffffffu, mbar_wait_bounded(s_full, gt & 1))) { ok = false; break; }
         tc_fence_after();
-      }
+        float sv[kN];
 #pragma unroll
-      for (int kb = 0; kb < kN / 64; ++kb) {
+        for (int c = 0; c < kN / 32; ++c) tmem_ld32(tmem_s + lane_base + c * 32, sv + c * 32);
+        tmem_wait_ld();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(s_free);
+        const int kbase = j * kN;
+        float mt = -INFINITY;
 #pragma unroll
-        for (int cc = 0; cc < 8; ++cc) {
-          const float *x = sv + kb * 64 + cc * 8;
-          uint4 w;
-          w.x = Pack2<T>::run(x[0], x[1]);
-          w.y = Pack2<T>::run(x[2], x[3]);
-          w.z = Pack2<T>::run(x[4], x[5]);
-          w.w = Pack2<T>::run(x[6], x[7]);
-          *reinterpret_cast<uint4 *>(prow + kb * (kM * 128) + swz(r, cc)) = w;
+        for (int c = 0; c < kN; ++c) {
+          sv[c] = (kbase + c < lim) ? sv[c] * p.scale_log2 : -INFINITY;
+          mt = fmaxf(mt, sv[c]);
         }
-      }
-      if (j > 0 && __any_sync(0xffffffffu, corr != 1.f)) {
+        // keep the old max unless this tile's exceeds it by > kRescaleLog2
+        const float m_new = (mt > m + kRescaleLog2 || m == -INFINITY) ? fmaxf(m, mt) : m;
+        const float ms = m_new == -INFINITY ? 0.f : m_new;
+        const float corr = m == m_new ? 1.f : fast_exp2(m - ms);
+        float sum = 0.f;
 #pragma unroll
-        for (int c = 0; c < D / 32; ++c) {
-          float ov[32];
-          tmem_ld32(tmem_o + lane_base + c * 32, ov);
-          tmem_wait_ld();
-#pragma unroll
-          for (int i = 0; i < 32; ++i) ov[i] *= corr;
-          tmem_st32(tmem_o + lane_base + c * 32, ov);
+        for (int c = 0; c < kN; ++c) {
+          sv[c] = fast_exp2(sv[c] - ms);
+          sum += sv[c];
         }
-        tmem_wait_st();
+        l = l * corr + sum;
+        m = m_new;
+        // the previous tile's P V must be done: P is rewritten, O rescaled
+        if (gt > 0) {
+          if (!__all_sync(0xffffffffu, mbar_wait_bounded(o_done, (gt - 1) & 1))) { ok = false; break; }
+          tc_fence_after();
+        }
+#pragma unroll
+        for (int kb = 0; kb < kN / 64; ++kb) {
+#pragma unroll
+          for (int cc = 0; cc < 8; ++cc) {
+            const float *x = sv + kb * 64 + cc * 8;
+            uint4 w;
+            w.x = Pack2<T>::run(x[0], x[1]);
+            w.y = Pack2<T>::run(x[2], x[3]);
+            w.z = Pack2<T>::run(x[4], x[5]);
+            w.w = Pack2<T>::run(x[6], x[7]);
+            *reinterpret_cast<uint4 *>(prow + kb * (kM * 128) + swz(r, cc)) = w;
+          }
+        }
+        if (j > 0 && __any_sync(0xffffffffu, corr != 1.f)) {
+#pragma unroll
+          for (int c = 0; c < D / 32; ++c) {
+            float ov[32];
+            tmem_ld32(tmem_o + lane_base + c * 32, ov);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) ov[i] *= corr;
+            tmem_st32(tmem_o + lane_base + c * 32, ov);
+          }
+          tmem_wait_st();
+        }
+        fence_proxy_async_smem();  // P visible to the tensor core
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(p_full);
       }
-      fence_proxy_async_smem();  // P visible to the tensor core
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(p_full);
-    }
-    // ---- epilogue -----------------------------------------------------------
-    if (__all_sync(0xffffffffu, ok && mbar_wait_bounded(o_done, (n_tiles - 1) & 1))) {
+      if (!ok) break;
+      // ---- epilogue: O of this item is complete once its last P V is -------
+      if (!__all_sync(0xffffffffu, mbar_wait_bounded(&o_full[ob], (oc >> 1) & 1))) {
+        ok = false;
+        break;
+      }
       tc_fence_after();
       const float inv = l > 0.f ? 1.f / l : 0.f;
-      T *o = static_cast<T *>(p.out) +
-             (static_cast<int64_t>(q_start + t0 + t) * p.hq + h * g + jh) * D;
+      T *o = static_cast<T *>(p.out) + orow * D;
 #pragma unroll
       for (int c = 0; c < D / 32; ++c) {
         float ov[32];
@@ -454,11 +563,11 @@ __global__ void __launch_bounds__(kThreadsP, 1)
           }
         }
       }
-      if (row_ok && p.lse)
-        p.lse[static_cast<int64_t>(q_start + t0 + t) * p.hq + h * g + jh] =
-            l > 0.f ? (m + __log2f(l)) * kLn2 : -INFINITY;
-    } else {
-      ok = false;
+      if (row_ok && p.lse) p.lse[orow] = l > 0.f ? (m + __log2f(l)) * kLn2 : -INFINITY;
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&o_free[ob]);  // O buffer ob may be overwritten
+      ++oc;
     }
   }
   if (!ok && lane == 0) flag(p.status, MI_STATUS_TIMEOUT);
@@ -466,8 +575,18 @@ __global__ void __launch_bounds__(kThreadsP, 1)
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(256)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                 "r"(L::TMEM_COLS)
                  : "memory");
+  }
+  // the last CTA out resets the shared item counters for the next launch
+  if (threadIdx.x == 0 && p.ctr) {
+    __threadfence();
+    if (atomicAdd(p.ctr + 1, 1u) + 1u == gridDim.x) {
+      p.ctr[0] = 0u;
+      p.ctr[1] = 0u;
+      __threadfence();
+    }
   }
 }
 
@@ -488,9 +607,10 @@ int launch_t(const PrefillParams &p, int dtype, cudaStream_t s) {
       return check_launch("prefill_tc_kernel smem attribute");
     attr_set |= 1ull << (dev & 63);
   }
-  // upper bound on (request, query tile) pairs: sum ceil(L_b / tq) <= total/tq + batch
-  const int tiles = (p.total_q + tq - 1) / tq + p.batch;
-  dim3 grid(tiles, p.hkv);
+  // persistent: one CTA per SM, or fewer when there are fewer work items
+  // (an upper bound on the items: (sum ceil(L_b / tq)) * hkv <= (total/tq + batch) * hkv)
+  const int64_t items = (static_cast<int64_t>(p.total_q) / tq + p.batch) * p.hkv;
+  const int grid = static_cast<int>(std::min<int64_t>(items, num_sms()));
   prefill_tc_kernel<T, D><<<grid, kThreadsP, L::SMEM, s>>>(qmap, kvmap, p);
   return check_launch("prefill_tc_kernel");
 }

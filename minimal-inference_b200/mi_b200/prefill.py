@@ -22,6 +22,11 @@ class BatchPrefillWithPagedKVCacheWrapper:
         if not float_workspace_buffer.is_cuda:
             raise capi.MiError("workspace must be a CUDA tensor (no CPU fallback)")
         self._ws = float_workspace_buffer
+        # the tensor-core kernel keeps two work-item counters at the start of
+        # the workspace; they must start at zero (each call leaves them so)
+        nbytes = self._ws.numel() * self._ws.element_size()
+        if nbytes >= 256:
+            self._ws.view(torch.uint8)[:256].zero_()
         self._plan = None
         self.status = torch.zeros(1, dtype=torch.int32, device=self._ws.device)
 

@@ -298,6 +298,33 @@ def test_prefill_ragged(dtype, hq, hkv, d, causal):
     np.testing.assert_allclose(lse, wlse, atol=max(TOL[dtype], 1e-3), rtol=0)
 
 
+@pytest.mark.parametrize("ws_bytes", [1 << 20, 16])
+def test_prefill_repeated_calls_share_workspace(ws_bytes):
+    """The persistent tensor-core prefill hands out work items through counters
+    in the workspace: three calls in a row on one workspace must each cover
+    every item (each call leaves the counters at zero); a workspace too small
+    for the counters selects the round-robin assignment instead."""
+    from mi_b200.prefill import BatchPrefillWithPagedKVCacheWrapper
+    kv_lens = [700, 37, 1300, 256, 90, 513]
+    hq, hkv, d, dtype = 32, 8, 128, "bfloat16"
+    c = paged_case(53, kv_lens, hq, hkv, d, dtype=dtype)
+    rng = np.random.default_rng(54)
+    q = po.round_to(rng.standard_normal((sum(kv_lens), hq, d), dtype=np.float32), dtype)
+    qo = np.concatenate([[0], np.cumsum(kv_lens)]).astype(np.int32)
+    want, _ = po.prefill_attention(q, qo, c["pool"], c["indptr"], c["indices"], c["last"], 16,
+                                   causal=True)
+    w = BatchPrefillWithPagedKVCacheWrapper(torch.empty(ws_bytes, dtype=torch.uint8, device=DEV))
+    w.plan(i32(qo), i32(c["indptr"]), i32(c["indices"]), i32(c["last"]), hq, hkv, d, c["ps"],
+           causal=True, q_data_type=tdt(dtype))
+    qd, pool = to_dev(q, dtype), to_dev(c["pool"], dtype)
+    for _ in range(3):
+        out = torch.full_like(qd, float("nan"))
+        w.run(qd, pool, out=out)
+        torch.cuda.synchronize()
+        w.check_status()
+        np.testing.assert_allclose(f32(out), want, atol=TOL[dtype], rtol=0)
+
+
 # --------------------------------------------------------------------------
 # the reference's own attention path, replayed through the GPU kernels
 # --------------------------------------------------------------------------
