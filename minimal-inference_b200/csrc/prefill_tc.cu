@@ -20,7 +20,8 @@
 //           mbarriers. S of tile j+1 is issued as soon as the softmax warps
 //           hold S of tile j in registers, so it runs under their softmax;
 //           P V of tile j follows once P is written;
-//   warps 2-5  softmax and epilogue: thread = TMEM lane = query row. Each KV
+//   warps 2-9  softmax and epilogue, two halves of four warps (S columns and
+//           O columns split between them): thread = TMEM lane = query row. Each KV
 //           tile: load the S row, causal/length mask, online softmax in the
 //           exp2 domain, write the bf16 P row into a 128-byte-swizzled tile,
 //           rescale the O row in TMEM only when the row max grew by more
@@ -39,7 +40,7 @@ namespace {
 
 constexpr int kM = 128;       // packed query rows per CTA
 constexpr int kN = 128;       // KV tokens per tile
-constexpr int kThreadsP = 192;
+constexpr int kThreadsP = 320;  // producer, MMA issuer, 2 x 4 softmax warps
 constexpr int kMaxBatchTc = 1024;
 
 template <int D> struct PfLayout {
@@ -52,9 +53,10 @@ template <int D> struct PfLayout {
   static constexpr int Q_OFF = 0;
   static constexpr int KV_OFF = Q_OFF + Q_BYTES;
   static constexpr int P_OFF = KV_OFF + 2 * STAGE_BYTES;
-  static constexpr int BAR_OFF = P_OFF + P_BYTES;      // 18 mbarriers + tmem base
+  static constexpr int BAR_OFF = P_OFF + P_BYTES;      // 24 mbarriers + tmem base
   static constexpr int ITEM_OFF = BAR_OFF + 256;       // 2 work-item records
-  static constexpr int META_OFF = ITEM_OFF + 64;
+  static constexpr int XCH_OFF = ITEM_OFF + 64;        // row max [2 tiles][2 halves][128], row sum [2][128]
+  static constexpr int META_OFF = XCH_OFF + (2 * 2 * kM + 2 * kM) * 4;
   static constexpr int SMEM = META_OFF + (kMaxBatchTc + 1) * 4 + 1024;
   // TMEM: S in [0, 128), O buffers at 128 and 128 + OB_STRIDE (head_dim wide)
   static constexpr int OB_STRIDE = D;
@@ -182,10 +184,14 @@ __global__ void __launch_bounds__(kThreadsP, 1)
   unsigned char *smem = reinterpret_cast<unsigned char *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L::BAR_OFF);
-  uint64_t *q_full = bars + 0, *q_empty = bars + 1, *kv_full = bars + 2, *kv_empty = bars + 4;
+  uint64_t *q_full = bars + 0, *q_empty = bars + 1;
+  // K and V tiles ride separate two-stage rings: a K stage frees as soon as
+  // its QK^T is done, so the next K load starts a softmax earlier than a V's
+  uint64_t *k_full = bars + 2, *k_empty = bars + 4, *v_full = bars + 20, *v_empty = bars + 22;
   uint64_t *s_full = bars + 6, *s_free = bars + 7, *p_full = bars + 8, *o_done = bars + 9;
   uint64_t *o_full = bars + 10, *o_free = bars + 12, *it_full = bars + 14, *it_empty = bars + 16;
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 18);
+  uint64_t *xch = bars + 18, *lxch = bars + 19;  // the two softmax halves' row max / row sum
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 24);
   PfItem *items = reinterpret_cast<PfItem *>(smem + L::ITEM_OFF);
   int *tiles_pre = reinterpret_cast<int *>(smem + L::META_OFF);
 
@@ -214,17 +220,21 @@ __global__ void __launch_bounds__(kThreadsP, 1)
       mbar_init(q_full, 1);
       mbar_init(q_empty, 1);
       for (int i = 0; i < 2; ++i) {
-        mbar_init(&kv_full[i], 1);
-        mbar_init(&kv_empty[i], 1);
+        mbar_init(&k_full[i], 1);
+        mbar_init(&k_empty[i], 1);
+        mbar_init(&v_full[i], 1);
+        mbar_init(&v_empty[i], 1);
         mbar_init(&o_full[i], 1);
-        mbar_init(&o_free[i], 4);
+        mbar_init(&o_free[i], 8);
         mbar_init(&it_full[i], 1);
-        mbar_init(&it_empty[i], 5);  // the MMA thread and the 4 softmax warps
+        mbar_init(&it_empty[i], 9);  // the MMA thread and the 8 softmax warps
       }
       mbar_init(s_full, 1);
-      mbar_init(s_free, 4);
-      mbar_init(p_full, 4);
+      mbar_init(s_free, 8);
+      mbar_init(p_full, 8);
       mbar_init(o_done, 1);
+      mbar_init(xch, 8);
+      mbar_init(lxch, 8);
     }
     __syncwarp();
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
@@ -296,51 +306,60 @@ __global__ void __launch_bounds__(kThreadsP, 1)
                       rec.q_start + rec.t0, q_full, pol_q);
       }
       ++qc;
-      const int nbox = 8 * 2 * DH;  // (16-token chunk, K/V, d block)
-      for (int j = 0; j < rec.n_tiles; ++j, ++gt) {
-        const int s = gt & 1;
+      // K or V (which) of tile j of this item, global tile index gtile, page
+      // ids of its eight 16-token chunks in lanes 0-7 of pg
+      auto issue = [&](int j, int gtile, int which, int pg) -> bool {
+        const int st = gtile & 1;
+        uint64_t *full = which ? &v_full[st] : &k_full[st];
+        uint64_t *empty = which ? &v_empty[st] : &k_empty[st];
+        if (gtile >= 2 &&
+            !__all_sync(0xffffffffu, mbar_wait_bounded(empty, ((gtile >> 1) - 1) & 1)))
+          return false;
         const int tok_tile = j * kN;
-        const int tok_c = tok_tile + lane * 16;  // page id of chunk c = lane (c < 8)
-        int pg = -1;
-        if (lane < 8 && tok_c < rec.lk) pg = p.indices[rec.page_base + tok_c / p.ps];
-        if (gt >= 2 && !__all_sync(0xffffffffu, mbar_wait_bounded(&kv_empty[s], ((gt >> 1) - 1) & 1))) {
-          ok = false;
-          break;
-        }
         const int nvc = min(8, cdiv(rec.lk - tok_tile, 16));
-        if (gt < 2 && nvc < 8) {
+        unsigned char *base = smem + L::KV_OFF + st * L::STAGE_BYTES + which * L::K_BYTES;
+        if (which == 1 && gtile < 2 && nvc < 8) {
           // V chunks past the request's end are multiplied by P = 0; on a
           // stage's first use they hold whatever shared memory held, so zero
           // them (later uses keep an earlier tile's finite values there)
           for (int dh = 0; dh < DH; ++dh) {
-            uint4 *v = reinterpret_cast<uint4 *>(smem + L::KV_OFF + s * L::STAGE_BYTES +
-                                                 L::K_BYTES + dh * (kN * 128) + nvc * 16 * 128);
+            uint4 *v = reinterpret_cast<uint4 *>(base + dh * (kN * 128) + nvc * 16 * 128);
             for (int i = lane; i < (8 - nvc) * 16 * 128 / 16; i += 32) v[i] = make_uint4(0, 0, 0, 0);
           }
           fence_proxy_async_smem();  // the zeros are visible to the tensor core
           __syncwarp();
         }
-        if (lane == 0) mbar_arrive_expect_tx(&kv_full[s], nvc * 2 * DH * 2048);
+        if (lane == 0) mbar_arrive_expect_tx(full, nvc * DH * 2048);
         __syncwarp();
-        const int c = min(lane / (2 * DH), 7), which = (lane / DH) & 1, dh = lane % DH;
+        const int c = min(lane / DH, 7), dh = lane % DH;
         const int page = __shfl_sync(0xffffffffu, pg, c);
-        if (lane < nbox && c < nvc) {
-          const int tok = tok_tile + c * 16;
+        if (lane < 8 * DH && c < nvc) {
           const bool bad = page < 0 || page >= p.num_pages;
-          unsigned char *dst = smem + L::KV_OFF + s * L::STAGE_BYTES + which * L::K_BYTES +
-                               dh * (kN * 128) + c * 16 * 128;
           // a bad page id loads from page 0 (in bounds) and is flagged; its
           // keys still count, so the result is wrong but nothing faults
-          tma_load_4d(dst, &kvmap, dh * 64, rec.h, tok % p.ps, (bad ? 0 : page) * 2 + which,
-                      &kv_full[s], pol_kv);
-          if (bad && which == 0 && dh == 0) flag(p.status, MI_STATUS_BAD_PAGE);
+          tma_load_4d(base + dh * (kN * 128) + c * 16 * 128, &kvmap, dh * 64, rec.h,
+                      (tok_tile + c * 16) % p.ps, (bad ? 0 : page) * 2 + which, full, pol_kv);
+          if (bad && dh == 0 && which == 0) flag(p.status, MI_STATUS_BAD_PAGE);
         }
+        return true;
+      };
+      // K runs one tile ahead of V: K0, K1, V0, K2, V1, ..., V(n-1)
+      int pg_prev = -1;
+      for (int j = 0; j < rec.n_tiles && ok; ++j, ++gt) {
+        const int tok_c = j * kN + lane * 16;  // page id of chunk c = lane (c < 8)
+        int pg = -1;
+        if (lane < 8 && tok_c < rec.lk) pg = p.indices[rec.page_base + tok_c / p.ps];
+        if (!issue(j, gt, 0, pg) || (j > 0 && !issue(j - 1, gt - 1, 1, pg_prev))) ok = false;
+        pg_prev = pg;
       }
+      if (ok && !issue(rec.n_tiles - 1, gt - 1, 1, pg_prev)) ok = false;
     }
     // no copy may be in flight when the CTA retires
     if (qc > 0 && !__all_sync(0xffffffffu, mbar_wait_bounded(q_full, (qc - 1) & 1))) ok = false;
     for (int t = max(0, gt - 2); t < gt; ++t)
-      if (!__all_sync(0xffffffffu, mbar_wait_bounded(&kv_full[t & 1], (t >> 1) & 1))) ok = false;
+      if (!__all_sync(0xffffffffu, mbar_wait_bounded(&k_full[t & 1], (t >> 1) & 1) &&
+                                       mbar_wait_bounded(&v_full[t & 1], (t >> 1) & 1)))
+        ok = false;
   } else if (warp == 1) {
     // ============================ MMA issuer ================================
     if (lane == 0) {
@@ -359,6 +378,7 @@ __global__ void __launch_bounds__(kThreadsP, 1)
                idesc_qk, kk > 0);
         }
         umma_commit(s_full);
+        umma_commit(&k_empty[t & 1]);
       };
       // Items come in order; the next item with keys is looked up ahead so
       // its first QK^T can run under the softmax of this item's last tile.
@@ -377,7 +397,7 @@ __global__ void __launch_bounds__(kThreadsP, 1)
       PfItem cur, nxt;
       bool have = next_item(cur), have_next = false;
       if (have) {  // first QK^T
-        if (!mbar_wait_bounded(q_full, 0) || !mbar_wait_bounded(&kv_full[0], 0)) ok = false;
+        if (!mbar_wait_bounded(q_full, 0) || !mbar_wait_bounded(&k_full[0], 0)) ok = false;
         if (ok) {
           tc_fence_after();
           issue_qk(0);
@@ -399,7 +419,7 @@ __global__ void __launch_bounds__(kThreadsP, 1)
           if (ahead) {
             if (!mbar_wait_bounded(s_free, gt & 1) ||
                 (cross && !mbar_wait_bounded(q_full, (qc + 1) & 1)) ||
-                !mbar_wait_bounded(&kv_full[(gt + 1) & 1], ((gt + 1) >> 1) & 1)) {
+                !mbar_wait_bounded(&k_full[(gt + 1) & 1], ((gt + 1) >> 1) & 1)) {
               ok = false;
               break;
             }
@@ -409,7 +429,11 @@ __global__ void __launch_bounds__(kThreadsP, 1)
             const bool last_qk = cross ? nxt.n_tiles == 1 : j + 2 == cur.n_tiles;
             if (last_qk) umma_commit(q_empty);
           }
-          if (!mbar_wait_bounded(p_full, gt & 1)) { ok = false; break; }
+          if (!mbar_wait_bounded(p_full, gt & 1) ||
+              !mbar_wait_bounded(&v_full[gt & 1], (gt >> 1) & 1)) {
+            ok = false;
+            break;
+          }
           if (j == 0 && oc >= 2 && !mbar_wait_bounded(&o_free[ob], ((oc >> 1) - 1) & 1)) {
             ok = false;
             break;
@@ -423,7 +447,7 @@ __global__ void __launch_bounds__(kThreadsP, 1)
             umma(tmem_o, umma_desc(p_addr + aoff, 16, 1024),
                  umma_desc(v_addr + kk * 16 * 128, kN * 128, 1024), idesc_pv, (j > 0 || kk > 0));
           }
-          umma_commit(&kv_empty[gt & 1]);
+          umma_commit(&v_empty[gt & 1]);
           umma_commit(o_done);
           if (j + 1 == cur.n_tiles) umma_commit(&o_full[ob]);
           last_gt = gt;
@@ -439,12 +463,21 @@ __global__ void __launch_bounds__(kThreadsP, 1)
     }
     __syncwarp();
   } else {
-    // ====================== softmax + epilogue (warps 2..5) =================
+    // ================ softmax + epilogue (warps 2..9) ========================
+    // Two halves of four warps each: the half sg owns S columns
+    // [64 sg, 64 sg + 64) (and so the P block sg) and O columns
+    // [D/2 sg, D/2 sg + D/2); thread = TMEM lane = packed query row in both.
+    // Per tile the halves swap their row maxima (xch), per item their row
+    // sums (lxch), through shared memory behind bounded mbarrier waits.
+    constexpr int SC = kN / 2, OC = D / 2;
+    const int sg = (warp - 2) >> 2;
     const int qd = warp & 3;
     const int r = qd * 32 + lane;  // packed row == TMEM lane
     const int t = r / g, jh = r % g;
     const uint32_t lane_base = static_cast<uint32_t>(qd * 32) << 16;
     unsigned char *prow = smem + L::P_OFF;
+    float *xmax = reinterpret_cast<float *>(smem + L::XCH_OFF);  // [tile & 1][half][row]
+    float *xsum = xmax + 4 * kM;                                  // [half][row]
     int gt = 0, oc = 0;
     for (int it = 0; ok; ++it) {
       const int slot = it & 1;
@@ -461,9 +494,9 @@ __global__ void __launch_bounds__(kThreadsP, 1)
       const int64_t orow = static_cast<int64_t>(rec.q_start + rec.t0 + t) * p.hq + rec.h * g + jh;
       if (rec.n_tiles == 0) {  // no visible key: zeros, lse = -inf
         if (row_ok) {
-          T *o = static_cast<T *>(p.out) + orow * D;
-          for (int i = 0; i < D; ++i) o[i] = Elt<T>::from(0.f);
-          if (p.lse) p.lse[orow] = -INFINITY;
+          T *o = static_cast<T *>(p.out) + orow * D + sg * OC;
+          for (int i = 0; i < OC; ++i) o[i] = Elt<T>::from(0.f);
+          if (p.lse && sg == 0) p.lse[orow] = -INFINITY;
         }
         continue;
       }
@@ -471,32 +504,41 @@ __global__ void __launch_bounds__(kThreadsP, 1)
       lim = min(lim, rec.lk);
       if (!row_ok) lim = 0;
       const int ob = oc & 1;
-      const uint32_t tmem_o = tmem + kN + ob * L::OB_STRIDE;
-      float m = -INFINITY, l = 0.f;
+      const uint32_t tmem_o = tmem + kN + ob * L::OB_STRIDE + sg * OC;
+      float m = -INFINITY, l = 0.f;  // l: this half's share of the row sum
       for (int j = 0; j < rec.n_tiles; ++j, ++gt) {
         if (!__all_sync(0xffffffffu, mbar_wait_bounded(s_full, gt & 1))) { ok = false; break; }
         tc_fence_after();
-        float sv[kN];
+        float sv[SC];
 #pragma unroll
-        for (int c = 0; c < kN / 32; ++c) tmem_ld32(tmem_s + lane_base + c * 32, sv + c * 32);
+        for (int c = 0; c < SC / 32; ++c)
+          tmem_ld32(tmem_s + sg * SC + lane_base + c * 32, sv + c * 32);
         tmem_wait_ld();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(s_free);
-        const int kbase = j * kN;
+        const int kbase = j * kN + sg * SC;
         float mt = -INFINITY;
 #pragma unroll
-        for (int c = 0; c < kN; ++c) {
+        for (int c = 0; c < SC; ++c) {
           sv[c] = (kbase + c < lim) ? sv[c] * p.scale_log2 : -INFINITY;
           mt = fmaxf(mt, sv[c]);
         }
+        // row max over both halves
+        float *xm = xmax + (gt & 1) * 2 * kM;
+        xm[sg * kM + r] = mt;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(xch);
+        if (!__all_sync(0xffffffffu, mbar_wait_bounded(xch, gt & 1))) { ok = false; break; }
+        mt = fmaxf(mt, xm[(sg ^ 1) * kM + r]);
         // keep the old max unless this tile's exceeds it by > kRescaleLog2
+        // (both halves see the same maxima, so they take the same decision)
         const float m_new = (mt > m + kRescaleLog2 || m == -INFINITY) ? fmaxf(m, mt) : m;
         const float ms = m_new == -INFINITY ? 0.f : m_new;
         const float corr = m == m_new ? 1.f : fast_exp2(m - ms);
         float sum = 0.f;
 #pragma unroll
-        for (int c = 0; c < kN; ++c) {
+        for (int c = 0; c < SC; ++c) {
           sv[c] = fast_exp2(sv[c] - ms);
           sum += sv[c];
         }
@@ -508,21 +550,18 @@ __global__ void __launch_bounds__(kThreadsP, 1)
           tc_fence_after();
         }
 #pragma unroll
-        for (int kb = 0; kb < kN / 64; ++kb) {
-#pragma unroll
-          for (int cc = 0; cc < 8; ++cc) {
-            const float *x = sv + kb * 64 + cc * 8;
-            uint4 w;
-            w.x = Pack2<T>::run(x[0], x[1]);
-            w.y = Pack2<T>::run(x[2], x[3]);
-            w.z = Pack2<T>::run(x[4], x[5]);
-            w.w = Pack2<T>::run(x[6], x[7]);
-            *reinterpret_cast<uint4 *>(prow + kb * (kM * 128) + swz(r, cc)) = w;
-          }
+        for (int cc = 0; cc < 8; ++cc) {
+          const float *x = sv + cc * 8;
+          uint4 w;
+          w.x = Pack2<T>::run(x[0], x[1]);
+          w.y = Pack2<T>::run(x[2], x[3]);
+          w.z = Pack2<T>::run(x[4], x[5]);
+          w.w = Pack2<T>::run(x[6], x[7]);
+          *reinterpret_cast<uint4 *>(prow + sg * (kM * 128) + swz(r, cc)) = w;
         }
         if (j > 0 && __any_sync(0xffffffffu, corr != 1.f)) {
 #pragma unroll
-          for (int c = 0; c < D / 32; ++c) {
+          for (int c = 0; c < OC / 32; ++c) {
             float ov[32];
             tmem_ld32(tmem_o + lane_base + c * 32, ov);
             tmem_wait_ld();
@@ -543,11 +582,19 @@ __global__ void __launch_bounds__(kThreadsP, 1)
         ok = false;
         break;
       }
+      xsum[sg * kM + r] = l;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(lxch);
+      if (!__all_sync(0xffffffffu, mbar_wait_bounded(lxch, oc & 1))) {
+        ok = false;
+        break;
+      }
+      l += xsum[(sg ^ 1) * kM + r];
       tc_fence_after();
       const float inv = l > 0.f ? 1.f / l : 0.f;
-      T *o = static_cast<T *>(p.out) + orow * D;
+      T *o = static_cast<T *>(p.out) + orow * D + sg * OC;
 #pragma unroll
-      for (int c = 0; c < D / 32; ++c) {
+      for (int c = 0; c < OC / 32; ++c) {
         float ov[32];
         tmem_ld32(tmem_o + lane_base + c * 32, ov);
         tmem_wait_ld();
@@ -563,7 +610,8 @@ __global__ void __launch_bounds__(kThreadsP, 1)
           }
         }
       }
-      if (row_ok && p.lse) p.lse[orow] = l > 0.f ? (m + __log2f(l)) * kLn2 : -INFINITY;
+      if (row_ok && p.lse && sg == 0)
+        p.lse[orow] = l > 0.f ? (m + __log2f(l)) * kLn2 : -INFINITY;
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&o_free[ob]);  // O buffer ob may be overwritten
