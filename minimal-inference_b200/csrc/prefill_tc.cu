@@ -57,7 +57,9 @@ template <int D> struct PfLayout {
   static constexpr int ITEM_OFF = BAR_OFF + 256;       // 2 work-item records
   static constexpr int XCH_OFF = ITEM_OFF + 64;        // row max [2 tiles][2 halves][128], row sum [2][128]
   static constexpr int META_OFF = XCH_OFF + (2 * 2 * kM + 2 * kM) * 4;
-  static constexpr int SMEM = META_OFF + (kMaxBatchTc + 1) * 4 + 1024;
+  // tiles_pre, qo_indptr, kv_indptr [batch+1] and kv_len [batch], in shared memory
+  static constexpr int META_INTS = 4 * (kMaxBatchTc + 1);
+  static constexpr int SMEM = META_OFF + META_INTS * 4 + 1024;
   // TMEM: S in [0, 128), O buffers at 128 and 128 + OB_STRIDE (head_dim wide)
   static constexpr int OB_STRIDE = D;
   static constexpr int TMEM_COLS = kN + 2 * D <= 256 ? 256 : 512;
@@ -194,6 +196,9 @@ __global__ void __launch_bounds__(kThreadsP, 1)
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 24);
   PfItem *items = reinterpret_cast<PfItem *>(smem + L::ITEM_OFF);
   int *tiles_pre = reinterpret_cast<int *>(smem + L::META_OFF);
+  int *s_qo = tiles_pre + (kMaxBatchTc + 1);       // qo_indptr
+  int *s_ip = s_qo + (kMaxBatchTc + 1);            // kv_indptr
+  int *s_lk = s_ip + (kMaxBatchTc + 1);            // kv length per request
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = p.group;
@@ -201,6 +206,11 @@ __global__ void __launch_bounds__(kThreadsP, 1)
   const int m_used = tq * g;    // packed rows in use
 
   // ---- once per CTA: query-tile prefix over requests, barriers, TMEM ------
+  for (int i = threadIdx.x; i <= p.batch; i += blockDim.x) {
+    s_qo[i] = p.qo_indptr[i];
+    s_ip[i] = p.indptr[i];
+    if (i < p.batch) s_lk[i] = kv_len_of(p.indptr, p.last, i, p.ps);
+  }
   if (warp == 0) {  // tiles_pre[i] = sum over b < i of ceil(qo_len_b / tq)
     int carry = 0;
     if (lane == 0) tiles_pre[0] = 0;
@@ -259,6 +269,8 @@ __global__ void __launch_bounds__(kThreadsP, 1)
     for (int it = 0; ok; ++it) {
       // next item: a counter shared by all CTAs (heaviest query tiles of each
       // request first), or round robin without a workspace
+      // next item: a counter shared by all CTAs (heaviest query tiles of each
+      // request first), or round robin without a workspace
       int k = 0;
       if (lane == 0) k = p.ctr ? static_cast<int>(atomicAdd(p.ctr, 1u)) : blockIdx.x + it * gridDim.x;
       k = __shfl_sync(0xffffffffu, k, 0);
@@ -274,10 +286,10 @@ __global__ void __launch_bounds__(kThreadsP, 1)
         rec.b = b;
         rec.h = rem / ntq;
         rec.t0 = (ntq - 1 - rem % ntq) * tq;
-        rec.q_start = p.qo_indptr[b];
-        rec.lq = p.qo_indptr[b + 1] - rec.q_start;
-        rec.lk = kv_len_of(p.indptr, p.last, b, p.ps);
-        rec.page_base = p.indptr[b];
+        rec.q_start = s_qo[b];
+        rec.lq = s_qo[b + 1] - rec.q_start;
+        rec.lk = s_lk[b];
+        rec.page_base = s_ip[b];
         const int rows_tok = min(tq, rec.lq - rec.t0);
         const int lim_tok =
             p.causal ? min(rec.lk, rec.lk - rec.lq + rec.t0 + rows_tok) : rec.lk;
@@ -294,6 +306,14 @@ __global__ void __launch_bounds__(kThreadsP, 1)
       }
       if (rec.b < 0) break;
       if (rec.n_tiles == 0) continue;
+      // page ids of 16-token chunks, 32 per window (four tiles), the current
+      // and the next window in registers; loaded before the Q wait below
+      const int nchunk = rec.n_tiles * 8;
+      auto load_win = [&](int w) -> int {
+        const int c = w * 32 + lane;
+        return c < nchunk && c * 16 < rec.lk ? p.indices[rec.page_base + (c * 16) / p.ps] : -1;
+      };
+      int pw = load_win(0), pwn = load_win(1);
       // Q tile into the single Q buffer once the previous item's last QK^T is done
       if (qc > 0 && !__all_sync(0xffffffffu, mbar_wait_bounded(q_empty, (qc - 1) & 1))) {
         ok = false;
@@ -306,9 +326,9 @@ __global__ void __launch_bounds__(kThreadsP, 1)
                       rec.q_start + rec.t0, q_full, pol_q);
       }
       ++qc;
-      // K or V (which) of tile j of this item, global tile index gtile, page
-      // ids of its eight 16-token chunks in lanes 0-7 of pg
-      auto issue = [&](int j, int gtile, int which, int pg) -> bool {
+      // K or V (which) of tile j of this item, global tile index gtile; page
+      // is this lane's chunk's page id (chunk lane / DH of the tile)
+      auto issue = [&](int j, int gtile, int which, int page) -> bool {
         const int st = gtile & 1;
         uint64_t *full = which ? &v_full[st] : &k_full[st];
         uint64_t *empty = which ? &v_empty[st] : &k_empty[st];
@@ -332,7 +352,6 @@ __global__ void __launch_bounds__(kThreadsP, 1)
         if (lane == 0) mbar_arrive_expect_tx(full, nvc * DH * 2048);
         __syncwarp();
         const int c = min(lane / DH, 7), dh = lane % DH;
-        const int page = __shfl_sync(0xffffffffu, pg, c);
         if (lane < 8 * DH && c < nvc) {
           const bool bad = page < 0 || page >= p.num_pages;
           // a bad page id loads from page 0 (in bounds) and is flagged; its
@@ -346,9 +365,11 @@ __global__ void __launch_bounds__(kThreadsP, 1)
       // K runs one tile ahead of V: K0, K1, V0, K2, V1, ..., V(n-1)
       int pg_prev = -1;
       for (int j = 0; j < rec.n_tiles && ok; ++j, ++gt) {
-        const int tok_c = j * kN + lane * 16;  // page id of chunk c = lane (c < 8)
-        int pg = -1;
-        if (lane < 8 && tok_c < rec.lk) pg = p.indices[rec.page_base + tok_c / p.ps];
+        if (j > 0 && (j & 3) == 0) {  // next window of page ids
+          pw = pwn;
+          pwn = load_win((j >> 2) + 1);
+        }
+        const int pg = __shfl_sync(0xffffffffu, pw, ((j & 3) << 3) + min(lane / DH, 7));
         if (!issue(j, gt, 0, pg) || (j > 0 && !issue(j - 1, gt - 1, 1, pg_prev))) ok = false;
         pg_prev = pg;
       }
