@@ -229,6 +229,102 @@ def model_decode(dev, batch=32, out_tokens=50, seed=3):
 
 
 # ---------------------------------------------------------------------------
+def churn_requests(n, vocab, seed=11, p_lo=64, p_hi=2048, o_lo=16, o_hi=512):
+    """BASELINE config 4's request stream: prompts U[p_lo, p_hi] of random ids,
+    output lengths U[o_lo, o_hi], seeded."""
+    rng = np.random.default_rng(seed)
+    return [(rng.integers(0, vocab, int(rng.integers(p_lo, p_hi + 1))).tolist(),
+             int(rng.integers(o_lo, o_hi + 1))) for _ in range(n)]
+
+
+def run_churn(args):
+    """Qwen2.5-7B-shape serving under churn.
+
+    max_batch 48, max_seq 4096, page_size 16; 48 requests start, and a new
+    one (prompt U[64,2048], output U[16,512], seeded) is submitted whenever
+    one finishes, until ``--batch`` requests (default 160) have been served,
+    so admissions, prefills, page growth and retirements interleave and the
+    pool fragments. Random bf16 weights, greedy, EOS disabled (outputs run to
+    their drawn length). Reports generated tokens per second of the whole
+    run, the reference-definition T2T and TTFT, and the decode step time.
+    """
+    import torch
+    from mi_b200.model import PRESETS, Model
+    from mi_b200.scheduler import Request, Scheduler
+
+    dev = torch.device("cuda", dist_env()[2])
+    torch.cuda.set_device(dev)
+    name = args.model or "qwen2.5-7b"
+    cfg = PRESETS[name]
+    n_req = args.batch or 160
+    model = Model.create(cfg, dev, torch.bfloat16, seed=7)
+    sched = Scheduler(model, cfg, dev, torch.bfloat16, max_batch_size=48, max_seq_len=4096,
+                      page_size=16, eos_token_ids=set())
+    stream = churn_requests(n_req, cfg.vocab_size)
+    # warm-up: a few short requests through every path (graph replay included)
+    warm = [Request(f"w{i}", p[:64], 4, 0.0) for i, (p, _) in enumerate(stream[:8])]
+    for r in warm:
+        sched.submit_request(r)
+    while sched.active_requests or sched.waiting_queue:
+        sched.step()
+    torch.cuda.synchronize()
+    reqs, nxt = [], 0
+
+    def submit(k):
+        nonlocal nxt
+        for _ in range(k):
+            if nxt >= n_req:
+                return
+            prompt, out_len = stream[nxt]
+            r = Request(f"r{nxt}", prompt, out_len, 0.0)
+            r.submit_time = time.perf_counter()
+            reqs.append(r)
+            sched.submit_request(r)
+            nxt += 1
+
+    clocks = ClockSampler(dist_env()[2])
+    t0 = time.perf_counter()
+    submit(48)
+    steps, step_ms, min_free = 0, [], sched.kv_cache.num_free_pages
+    while sched.active_requests or sched.waiting_queue or nxt < n_req:
+        done_before = sum(1 for r in reqs if r.status.value == "finished")
+        ts = time.perf_counter()
+        sched.step()
+        step_ms.append((time.perf_counter() - ts) * 1e3)
+        steps += 1
+        min_free = min(min_free, sched.kv_cache.num_free_pages)
+        done = sum(1 for r in reqs if r.status.value == "finished")
+        submit(done - done_before)   # a new request whenever a slot frees
+    torch.cuda.synchronize()
+    wall = time.perf_counter() - t0
+    clk = clocks.stop()
+    sched.kv_cache.check_status()
+    gen = sum(len(r.generated_tokens) for r in reqs)
+    t2t = [(r.last_token_time - r.prefill_done_time) / (len(r.generated_tokens) - 1)
+           for r in reqs if len(r.generated_tokens) > 1]
+    ttft = [r.prefill_done_time - r.submit_time for r in reqs]
+    complete = all(len(r.generated_tokens) == stream[i][1] for i, r in enumerate(reqs))
+    pages_back = int(sched.kv_cache.pool_ctrl[1].item()) == sched.kv_cache.max_num_pages - 1
+    sched.close()
+    line = {"metric": f"{name} serving under churn: generated tok/s (config 4)",
+            "value": round(gen / wall, 1), "unit": "tok/s", "n_gpus": 1, "steps": steps,
+            "warmup": len(warm), "ms_per_step": round(statistics.median(step_ms), 3),
+            "higher_is_better": True, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "continuous batching with a new request whenever one "
+                                   "finishes", "model": name, "max_batch": 48,
+                       "max_seq_len": 4096, "requests": n_req,
+                       "prompt_lens": "U[64,2048]", "output_lens": "U[16,512]",
+                       "page_size": 16, "weights": "random N(0,0.02) bf16"},
+            "t2t_ms_mean": round(statistics.mean(t2t) * 1e3, 3),
+            "ttft_ms_mean": round(statistics.mean(ttft) * 1e3, 1),
+            "generated_tokens": gen, "wall_s": round(wall, 3),
+            "min_free_pages": min_free, "pool_pages": sched.kv_cache.max_num_pages,
+            "all_outputs_complete": complete, "all_pages_returned": pages_back,
+            "clocks": clk}
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------
 def run_tp_decode(args):
     """Qwen2.5-72B-shape continuous-batching decode with
     tensor parallelism over the N GPUs of the launch (one rank per GPU, NCCL).
@@ -510,12 +606,14 @@ def parse_args():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-model", action="store_true",
                     help="skip the Mistral-7B-shape decode measurement (config 3)")
-    ap.add_argument("--workload", choices=["config2", "config5", "prefill", "decode-shapes"],
+    ap.add_argument("--workload",
+                    choices=["config2", "config4", "config5", "prefill", "decode-shapes"],
                     default="config2",
                     help="config5: Qwen2.5-72B tensor-parallel decode over the launch's GPUs; "
                          "prefill: the paged prefill kernel alone on config 3's prompts")
     ap.add_argument("--model", default=None, help="config5: model preset (default qwen2.5-72b)")
-    ap.add_argument("--batch", type=int, default=None, help="config5: requests (default 64)")
+    ap.add_argument("--batch", type=int, default=None,
+                    help="config5: requests (default 64); config4: requests served (default 160)")
     ap.add_argument("--decode-steps", type=int, default=None,
                     help="config5: decode steps per request (default 128)")
     return ap.parse_args()
@@ -572,6 +670,9 @@ def main():
         return
     if args.workload == "config5":
         run_tp_decode(args)
+        return
+    if args.workload == "config4":
+        run_churn(args)
         return
     if args.workload == "prefill":
         run_prefill(args)
