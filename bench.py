@@ -357,6 +357,8 @@ def run_tp_decode(args):
     t0 = time.perf_counter()
     model = Model.create(cfg, dev, torch.bfloat16, seed=5, tp_rank=rank, tp_size=world,
                          tp_group=group)
+    if world > 1 and args.allreduce == "peer":
+        model.enable_peer_allreduce(max_rows=batch)
     torch.cuda.synchronize()
     init_s = time.perf_counter() - t0
     rng = np.random.default_rng(5)
@@ -401,6 +403,8 @@ def run_tp_decode(args):
     t2t, dec_ms, first_s, init_s, capture_s = max_over_ranks(
         [t2t, dec_ms, first_s, init_s, capture_s])
     ok = all(len(r.generated_tokens) == steps + 1 for r in reqs)
+    if model.comm is not None:
+        model.comm.check_status()
     sched.close()
     del sched, model
     if world > 1:
@@ -417,7 +421,8 @@ def run_tp_decode(args):
                                "admitted at once, greedy", "model": name,
                    "global_batch": batch, "seq_len": f"prompts U[{lo},{hi}] + {steps} decode",
                    "parallelism": f"tp{world}", "page_size": 16,
-                   "weights": "random N(0,0.02) bf16"},
+                   "weights": "random N(0,0.02) bf16",
+                   "decode_allreduce": (args.allreduce if world > 1 else "none")},
         "first_step_s (prefill of all + 1 decode)": round(first_s, 3),
         "model_init_s": round(init_s, 2), "graph_capture_s": round(capture_s, 2),
         "decode_steps_timed": n_dec, "all_requests_complete": ok, "clocks": clk,
@@ -616,6 +621,9 @@ def parse_args():
                     help="config5: requests (default 64); config4: requests served (default 160)")
     ap.add_argument("--decode-steps", type=int, default=None,
                     help="config5: decode steps per request (default 128)")
+    ap.add_argument("--allreduce", choices=["peer", "nccl"], default="peer",
+                    help="config5: decode-step all-reduce: fused over NVLink peer memory "
+                         "(with the residual add and RMSNorm) or NCCL")
     return ap.parse_args()
 
 

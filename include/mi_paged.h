@@ -271,6 +271,31 @@ int mi_add_rmsnorm(const void *x, void *residual, const void *weight, void *out,
 int mi_silu_mul(const void *gate_up, void *out, int32_t rows, int32_t inter, int32_t dtype,
                 mi_stream_t stream);
 
+/* ---- tensor parallelism: fused all-reduce for decode steps --------------- */
+
+/* No FlashInfer counterpart: replaces, for decode-sized row counts, the
+ * torch.distributed all_reduce after a row-parallel o_proj / down_proj plus
+ * the residual add and RMSNorm that follow it (model.py:115-122, :333-343).
+ *
+ * Every rank owns a symmetric buffer (same size; each rank's buffer mapped
+ * into every rank's address space); peer_bases[q] (a device array of
+ * `world` 64-bit addresses) is rank q's buffer as this process sees it. At
+ * byte offset data_off every rank's GEMM has written its partial
+ * [rows][hidden] sum before this call; at flag_off lies a uint32 array
+ * [world][256], zero-filled on every rank (and all ranks past a barrier)
+ * before the first call. block_counters: this rank's uint32 [256], zeroed
+ * once. Then: residual[r] += sum over ranks of partial[r] (rounded to dtype
+ * as the all-reduce result, then as the add), out[r] = rms_norm(residual[r])
+ * * weight. rows <= 256. Every rank must make the same sequence of calls
+ * (same rows); a call site's partial must not be rewritten before this
+ * rank's next call has returned. Waits for peers are bounded (10 s): on
+ * give-up MI_STATUS_TIMEOUT is set and the outputs are not written. */
+int mi_allreduce_add_rmsnorm(const unsigned long long *peer_bases, int64_t data_off,
+                             int64_t flag_off, uint32_t *block_counters, int32_t rank,
+                             int32_t world, void *residual, const void *weight, void *out,
+                             int32_t rows, int32_t hidden, float eps, int32_t dtype,
+                             int32_t *status, mi_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -72,6 +72,8 @@ _SIGS = {
                         ctypes.c_int),
     "mi_add_rmsnorm": ([_c_p, _c_p, _c_p, _c_p, _c_i32, _c_i32, _c_f, _c_i32, _c_p], ctypes.c_int),
     "mi_silu_mul": ([_c_p, _c_p, _c_i32, _c_i32, _c_i32, _c_p], ctypes.c_int),
+    "mi_allreduce_add_rmsnorm": ([_c_p, _c_i64, _c_i64, _c_p, _c_i32, _c_i32, _c_p, _c_p, _c_p,
+                                 _c_i32, _c_i32, _c_f, _c_i32, _c_p, _c_p], ctypes.c_int),
 }
 
 _lib = None

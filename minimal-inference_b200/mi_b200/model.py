@@ -145,7 +145,10 @@ class Attention(nn.Module):
             self._qkv_b = (_fuse_rows([p.bias for p in projs])
                            if self.q_proj.bias is not None else None)
 
-    def forward(self, x, cos, sin, mask, kv_cache=None, position_ids=None, attn_backend=None):
+    def forward(self, x, cos, sin, mask, kv_cache=None, position_ids=None, attn_backend=None,
+                *, proj_out: torch.Tensor | None = None):
+        """``proj_out`` (extension): ``[tokens, hidden]`` buffer the o_proj GEMM
+        writes into (the tensor-parallel peer all-reduce reads it from there)."""
         if attn_backend is None:
             raise RuntimeError("mi_b200 has no padded/CPU attention path: pass attn_backend")
         bsz, seq_len, _ = x.shape
@@ -168,6 +171,9 @@ class Attention(nn.Module):
                               rope_cos=be.rope_cos, rope_sin=be.rope_sin, q=q, q_out=q_rot,
                               scratch_page=be.paged_kv_cache.scratch_page, status=be.status)
         out = be.wrapper.run(q_rot, kv_data, out=be.out_buffer(n, hq, d, x.dtype))
+        if proj_out is not None:
+            torch.mm(out.view(n, hq * d), self.o_proj.weight.t(), out=proj_out)
+            return proj_out.view(bsz, seq_len, -1)
         return self.o_proj(out.view(bsz, seq_len, hq * d))
 
 
@@ -186,10 +192,14 @@ class MLP(nn.Module):
         with torch.no_grad():
             self._gu_w = _fuse_rows([self.gate_proj.weight, self.up_proj.weight])
 
-    def forward(self, x: torch.Tensor) -> torch.Tensor:
+    def forward(self, x: torch.Tensor, *, proj_out: torch.Tensor | None = None) -> torch.Tensor:
         if self._gu_w is None:
             self.fuse()
-        return self.down_proj(silu_mul(F.linear(x, self._gu_w)))
+        act = silu_mul(F.linear(x, self._gu_w))
+        if proj_out is not None:  # down_proj straight into a peer all-reduce region
+            torch.mm(act.view(-1, act.shape[-1]), self.down_proj.weight.t(), out=proj_out)
+            return proj_out.view(*act.shape[:-1], -1)
+        return self.down_proj(act)
 
 
 class DecoderLayer(nn.Module):
@@ -200,6 +210,8 @@ class DecoderLayer(nn.Module):
         self.post_attention_layernorm = RMSNorm(config.hidden_size, config.rms_norm_eps)
         self.mlp = MLP(config, shard.get("intermediate_size"))
         self.tp_size, self.tp_group = tp_size, tp_group
+        self.layer_idx = 0
+        self.comm = None  # PeerAllReduce, when the fused decode all-reduce is enabled
 
     def _reduce(self, x: torch.Tensor) -> torch.Tensor:
         """Sum of the row-parallel partial outputs over the tensor-parallel ranks."""
@@ -210,20 +222,40 @@ class DecoderLayer(nn.Module):
     def forward(self, x, cos, sin, mask, kv_cache=None, position_ids=None, attn_backend=None):
         """Reference signature (model.py:322-343); returns the new residual."""
         h = x.contiguous().clone()
-        h.add_(self.residual_step(h, None, position_ids, attn_backend))
+        x_out, site = self.residual_step(h, None, position_ids, attn_backend)
+        add_norm(self.comm, (x_out, site), h, self.input_layernorm)  # only for the add
         return h
 
     def residual_step(self, h, pending, position_ids, attn_backend):
         """One layer on the residual stream ``h`` (updated in place).
 
         ``pending`` is the previous layer's MLP output not yet added to ``h``
-        (None for the first layer); the add runs fused into this layer's input
-        RMSNorm. Returns this layer's MLP output, likewise not yet added."""
-        y = add_rmsnorm(pending, h, self.input_layernorm.weight, self.input_layernorm.eps)
-        a = self._reduce(self.self_attn(y, None, None, None, None, position_ids, attn_backend))
-        y = add_rmsnorm(a, h, self.post_attention_layernorm.weight,
-                        self.post_attention_layernorm.eps)
-        return self._reduce(self.mlp(y))
+        (None for the first layer) as ``(tensor, site)``: site None means the
+        tensor is complete, else it is this rank's partial in peer all-reduce
+        region ``site``. The add (and the reduction) runs fused into this
+        layer's input RMSNorm. Returns this layer's MLP output, likewise."""
+        rows = h.numel() // h.shape[-1]
+        peer = self.comm is not None and self.comm.usable(rows)
+        y = add_norm(self.comm, pending, h, self.input_layernorm)
+        site_a, site_m = 2 * self.layer_idx, 2 * self.layer_idx + 1
+        a = self.self_attn(y, None, None, None, None, position_ids, attn_backend,
+                           proj_out=self.comm.site(site_a, rows) if peer else None)
+        y = add_norm(self.comm, (a, site_a) if peer else (self._reduce(a), None), h,
+                     self.post_attention_layernorm)
+        m = self.mlp(y, proj_out=self.comm.site(site_m, rows) if peer else None)
+        return (m, site_m) if peer else (self._reduce(m), None)
+
+
+def add_norm(comm, pending, h: torch.Tensor, norm: "RMSNorm") -> torch.Tensor:
+    """``h += pending`` (all-reduced first when it is a peer partial), then
+    ``norm(h)``; see ``DecoderLayer.residual_step``."""
+    if pending is None:
+        return add_rmsnorm(None, h, norm.weight, norm.eps)
+    x, site = pending
+    if site is None:
+        return add_rmsnorm(x, h, norm.weight, norm.eps)
+    rows = h.numel() // h.shape[-1]
+    return comm.reduce_add_norm(site, rows, h, norm.weight, norm.eps)
 
 
 def tp_shard_sizes(config: ModelConfig, tp_size: int) -> dict:
@@ -286,6 +318,7 @@ class Model(nn.Module):
         self.lm_head = (None if config.tie_word_embeddings else
                         nn.Linear(config.hidden_size, vocab_local, bias=False))
         self.vocab_local = vocab_local
+        self.comm = None
         # fp32 tables built exactly as model.py:79-89, cast with the model
         cos, sin = rope_tables(config.head_dim, config.max_position_embeddings,
                                config.rope_theta)
@@ -297,6 +330,22 @@ class Model(nn.Module):
         for layer in self.layers:
             layer.self_attn.fuse()
             layer.mlp.fuse()
+        return self
+
+    def enable_peer_allreduce(self, max_rows: int = 64) -> "Model":
+        """Decode steps of up to ``max_rows`` tokens reduce the row-parallel
+        partials over NVLink peer memory, fused with the residual add and
+        RMSNorm (``tp_comm.PeerAllReduce``); longer forwards keep NCCL."""
+        if self.tp_size == 1:
+            return self
+        from .tp_comm import PeerAllReduce
+        dtype = self.norm.weight.dtype
+        self.comm = PeerAllReduce(self.tp_group or torch.distributed.group.WORLD,
+                                  self.norm.weight.device, dtype, self.config.hidden_size,
+                                  2 * len(self.layers), max_rows)
+        for i, layer in enumerate(self.layers):
+            layer.layer_idx = i
+            layer.comm = self.comm
         return self
 
     @classmethod
@@ -341,7 +390,7 @@ class Model(nn.Module):
             pending = layer.residual_step(h, pending, position_ids, attn_backend)
         # last residual add + final norm; the norm is per row, so selecting
         # rows after it equals selecting before
-        h = add_rmsnorm(pending, h, self.norm.weight, self.norm.eps)
+        h = add_norm(self.comm, pending, h, self.norm)
         if logits_rows is not None:
             h = h.reshape(-1, h.shape[-1])[logits_rows].unsqueeze(0)
         return gather_vocab_logits(F.linear(h, self._lm_head_weight()), self.tp_size,

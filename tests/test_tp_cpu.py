@@ -2,7 +2,6 @@
 random init, and the column/row-parallel split with its all-reduce and the
 vocab all-gather, run as two gloo ranks against the unsharded model."""
 import multiprocessing as mp
-import socket
 
 import pytest
 import torch
@@ -51,17 +50,11 @@ def test_sharded_init_holds_slices_of_the_full_weights():
             assert torch.equal(p, want), name
 
 
-def _free_port() -> int:
-    with socket.socket() as s:
-        s.bind(("127.0.0.1", 0))
-        return s.getsockname()[1]
-
-
-def test_tp2_gloo_matches_dense_model():
+def test_tp2_gloo_matches_dense_model(tmp_path):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    port = _free_port()
-    procs = [ctx.Process(target=tp_decomposition, args=(r, 2, port, q)) for r in range(2)]
+    init_file = str(tmp_path / "gloo_rendezvous")
+    procs = [ctx.Process(target=tp_decomposition, args=(r, 2, init_file, q)) for r in range(2)]
     for p in procs:
         p.start()
     results = dict(q.get(timeout=240) for _ in procs)

@@ -11,7 +11,6 @@ shards), and every prefill and decode logits row must match the one-GPU run
 within max-abs 1e-3.
 """
 import multiprocessing as mp
-import socket
 
 import numpy as np
 import pytest
@@ -20,15 +19,9 @@ torch = pytest.importorskip("torch")
 pytestmark = pytest.mark.gpu
 
 
-def _free_port() -> int:
-    with socket.socket() as s:
-        s.bind(("127.0.0.1", 0))
-        return s.getsockname()[1]
-
-
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2,
                     reason="needs two GPUs")
-def test_tp2_decode_matches_single_gpu():
+def test_tp2_decode_matches_single_gpu(tmp_path):
     from mi_b200.model import Model
     from tests.tp_workers import _gpu_small_cfg, run_scheduler_logits, tp_gpu_decode
 
@@ -44,8 +37,8 @@ def test_tp2_decode_matches_single_gpu():
 
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    port = _free_port()
-    procs = [ctx.Process(target=tp_gpu_decode, args=(r, 2, port, prompts, max_new, toks1, q))
+    init_file = str(tmp_path / "nccl_rendezvous")
+    procs = [ctx.Process(target=tp_gpu_decode, args=(r, 2, init_file, prompts, max_new, toks1, q))
              for r in range(2)]
     for p in procs:
         p.start()
@@ -65,3 +58,41 @@ def test_tp2_decode_matches_single_gpu():
         assert torch.equal(b0, b1)                    # ranks agree bit for bit
         worst = max(worst, float((a - b0).abs().max()))
     assert worst <= 1e-3, worst
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2,
+                    reason="needs two GPUs")
+def test_tp2_peer_allreduce_matches_nccl(tmp_path):
+    """The fused peer-memory all-reduce + residual add + RMSNorm of decode
+    steps against the NCCL all-reduce + add_rmsnorm path, bf16, both ranks:
+    logits within one bf16 rounding of the (small) logits, ranks identical."""
+    from tests.tp_workers import _gpu_small_cfg, tp_gpu_peer_vs_nccl
+
+    cfg = _gpu_small_cfg()
+    rng = np.random.default_rng(6)
+    prompts = [rng.integers(0, cfg.vocab_size, n).tolist() for n in (20, 64, 130)]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    init_file = str(tmp_path / "nccl_rendezvous")
+    procs = [ctx.Process(target=tp_gpu_peer_vs_nccl, args=(r, 2, init_file, prompts, 10, q))
+             for r in range(2)]
+    for p in procs:
+        p.start()
+    got = {}
+    for _ in procs:
+        rank, ta, la, tb, lb = q.get(timeout=600)
+        got[rank] = (ta, la, tb, lb)
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    ta, la, tb, lb = got[0]
+    assert tb == ta and got[1][2] == ta
+    worst = 0.0
+    for (ka, ia, xa), (kb, ib, xb), (_, _, xb1) in zip(la, lb, got[1][3]):
+        assert ka == kb and ia == ib
+        assert torch.equal(xb, xb1)
+        if ka == "decode":        # prefill rows take the NCCL path in both runs
+            worst = max(worst, float((xa - xb).abs().max()))
+        else:
+            assert torch.equal(xa, xb)
+    assert worst <= 2.0 ** -4, worst

@@ -18,11 +18,11 @@ def _mlp(m, x):
 
 
 @torch.no_grad()
-def tp_decomposition(rank: int, world: int, port: int, out_q) -> None:
+def tp_decomposition(rank: int, world: int, init_file: str, out_q) -> None:
     """Each rank's shard, combined through the collectives the model uses,
     against the unsharded model's dense math on the same seeded weights."""
-    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
-    dist.init_process_group("gloo", rank=rank, world_size=world)
+    dist.init_process_group("gloo", init_method=f"file://{init_file}", rank=rank,
+                            world_size=world)
     try:
         cfg = TINY
         full = Model(cfg)
@@ -85,22 +85,47 @@ def run_scheduler_logits(model, cfg, dev, prompts, max_new, teacher=None):
     return toks, logs
 
 
-@torch.no_grad()
-def tp_gpu_decode(rank: int, world: int, port: int, prompts, max_new, teacher, out_q) -> None:
+def _nccl_init(rank: int, world: int, init_file: str):
     from datetime import timedelta
-
-    from mi_b200.model import Model
-
-    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dev = torch.device("cuda", rank)
     torch.cuda.set_device(dev)
-    dist.init_process_group("nccl", rank=rank, world_size=world,
-                            timeout=timedelta(seconds=120), device_id=dev)
+    dist.init_process_group("nccl", init_method=f"file://{init_file}", rank=rank,
+                            world_size=world, timeout=timedelta(seconds=120), device_id=dev)
+    return dev
+
+
+@torch.no_grad()
+def tp_gpu_decode(rank: int, world: int, init_file: str, prompts, max_new, teacher,
+                  out_q) -> None:
+    from mi_b200.model import Model
+
+    dev = _nccl_init(rank, world, init_file)
     try:
         cfg = _gpu_small_cfg()
         model = Model.create(cfg, dev, torch.float32, seed=21, tp_rank=rank, tp_size=world,
                              tp_group=dist.group.WORLD)
         toks, logs = run_scheduler_logits(model, cfg, dev, prompts, max_new, teacher)
         out_q.put((rank, toks, [(k, ids, rows) for k, ids, rows in logs]))
+    finally:
+        dist.destroy_process_group()
+
+
+@torch.no_grad()
+def tp_gpu_peer_vs_nccl(rank: int, world: int, init_file: str, prompts, max_new, out_q) -> None:
+    """bf16 TP decode twice on the same model: NCCL all-reduce, then the fused
+    peer-memory all-reduce (teacher-forced with the first run's tokens)."""
+    from mi_b200.model import Model
+
+    dev = _nccl_init(rank, world, init_file)
+    try:
+        cfg = _gpu_small_cfg()
+        model = Model.create(cfg, dev, torch.bfloat16, seed=21, tp_rank=rank, tp_size=world,
+                             tp_group=dist.group.WORLD)
+        toks_a, logs_a = run_scheduler_logits(model, cfg, dev, prompts, max_new)
+        model.enable_peer_allreduce(max_rows=8)
+        toks_b, logs_b = run_scheduler_logits(model, cfg, dev, prompts, max_new, teacher=toks_a)
+        torch.cuda.synchronize()
+        model.comm.check_status()
+        out_q.put((rank, toks_a, logs_a, toks_b, logs_b))
     finally:
         dist.destroy_process_group()
