@@ -357,7 +357,10 @@ def run_tp_decode(args):
     t0 = time.perf_counter()
     model = Model.create(cfg, dev, torch.bfloat16, seed=5, tp_rank=rank, tp_size=world,
                          tp_group=group)
-    if world > 1 and args.allreduce == "peer":
+    allreduce = args.allreduce
+    if allreduce == "auto":
+        allreduce = "peer" if world <= 4 else "nccl"
+    if world > 1 and allreduce == "peer":
         model.enable_peer_allreduce(max_rows=batch)
     torch.cuda.synchronize()
     init_s = time.perf_counter() - t0
@@ -415,6 +418,9 @@ def run_tp_decode(args):
         "metric": f"{name} decode tok/s @B={batch}, tensor parallel (config 5)",
         "value": round(batch / (t2t / 1e3), 1), "unit": "tok/s", "n_gpus": world,
         "steps": steps, "warmup": 0, "ms_per_step": round(dec_ms, 3), "t2t_ms": round(t2t, 3),
+        "decode_step_tok_s": round(batch / (dec_ms / 1e3), 1),
+        "t2t_note": ("reference definition (per request, first to last token): includes the "
+                     "wait of early-prefilled requests for the later prefill chunks"),
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic",
         "config": {"workload": "BASELINE config 5: continuous-batching decode, all requests "
@@ -422,7 +428,7 @@ def run_tp_decode(args):
                    "global_batch": batch, "seq_len": f"prompts U[{lo},{hi}] + {steps} decode",
                    "parallelism": f"tp{world}", "page_size": 16,
                    "weights": "random N(0,0.02) bf16",
-                   "decode_allreduce": (args.allreduce if world > 1 else "none")},
+                   "decode_allreduce": (allreduce if world > 1 else "none")},
         "first_step_s (prefill of all + 1 decode)": round(first_s, 3),
         "model_init_s": round(init_s, 2), "graph_capture_s": round(capture_s, 2),
         "decode_steps_timed": n_dec, "all_requests_complete": ok, "clocks": clk,
@@ -621,9 +627,10 @@ def parse_args():
                     help="config5: requests (default 64); config4: requests served (default 160)")
     ap.add_argument("--decode-steps", type=int, default=None,
                     help="config5: decode steps per request (default 128)")
-    ap.add_argument("--allreduce", choices=["peer", "nccl"], default="peer",
+    ap.add_argument("--allreduce", choices=["auto", "peer", "nccl"], default="auto",
                     help="config5: decode-step all-reduce: fused over NVLink peer memory "
-                         "(with the residual add and RMSNorm) or NCCL")
+                         "(with the residual add and RMSNorm), NCCL, or auto (peer up to "
+                         "4 GPUs, NCCL beyond: there NCCL's in-switch reduction wins)")
     return ap.parse_args()
 
 

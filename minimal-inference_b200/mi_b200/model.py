@@ -339,6 +339,7 @@ class Model(nn.Module):
         if self.tp_size == 1:
             return self
         from .tp_comm import PeerAllReduce
+        self.requires_grad_(False)  # the projections write into the peer buffers (out=)
         dtype = self.norm.weight.dtype
         self.comm = PeerAllReduce(self.tp_group or torch.distributed.group.WORLD,
                                   self.norm.weight.device, dtype, self.config.hidden_size,
@@ -367,6 +368,7 @@ class Model(nn.Module):
         model.sin_cached = sin.to(dtype).to(device)
         if seed is not None:
             init_random_weights(model, seed, generator_device=torch.device(device).type)
+        model.requires_grad_(False)  # an inference model (GEMMs may write into given buffers)
         return model.eval().prepare()
 
     def _lm_head_weight(self) -> torch.Tensor:
