@@ -16,7 +16,7 @@
 //           two K/V stages, 128-byte swizzle;
 //   warp 1  MMA issuer (one thread): S = Q K^T into TMEM (M=128, N=128,
 //           K=head_dim, both operands K-major), then O += P V into TMEM
-//           (P K-major from shared memory, V MN-major), tcgen05.commit to
+//           (P K-major from TMEM, V MN-major from shared memory), tcgen05.commit to
 //           mbarriers. S of tile j+1 is issued as soon as the softmax warps
 //           hold S of tile j in registers, so it runs under their softmax;
 //           P V of tile j follows once P is written;
@@ -49,20 +49,21 @@ template <int D> struct PfLayout {
   static constexpr int K_BYTES = DH * kN * 128;       // [dh][token][64]
   static constexpr int V_BYTES = K_BYTES;
   static constexpr int STAGE_BYTES = K_BYTES + V_BYTES;
-  static constexpr int P_BYTES = (kN / 64) * kM * 128;  // [kblock][row][64]
-  static constexpr int Q_OFF = 0;
-  static constexpr int KV_OFF = Q_OFF + Q_BYTES;
-  static constexpr int P_OFF = KV_OFF + 2 * STAGE_BYTES;
-  static constexpr int BAR_OFF = P_OFF + P_BYTES;      // 24 mbarriers + tmem base
+  static constexpr int Q_OFF = 0;                      // two Q buffers (items alternate)
+  static constexpr int KV_OFF = Q_OFF + 2 * Q_BYTES;
+  static constexpr int BAR_OFF = KV_OFF + 2 * STAGE_BYTES;  // 28 mbarriers + tmem base
   static constexpr int ITEM_OFF = BAR_OFF + 256;       // 2 work-item records
   static constexpr int XCH_OFF = ITEM_OFF + 64;        // row max [2 tiles][2 halves][128], row sum [2][128]
   static constexpr int META_OFF = XCH_OFF + (2 * 2 * kM + 2 * kM) * 4;
   // tiles_pre, qo_indptr, kv_indptr [batch+1] and kv_len [batch], in shared memory
   static constexpr int META_INTS = 4 * (kMaxBatchTc + 1);
   static constexpr int SMEM = META_OFF + META_INTS * 4 + 1024;
-  // TMEM: S in [0, 128), O buffers at 128 and 128 + OB_STRIDE (head_dim wide)
+  // TMEM columns: S [0, 128) fp32; P [128, 192) as bf16 pairs (the A operand
+  // of P V); two O buffers of head_dim columns from 192
+  static constexpr int P_COL = kN;
+  static constexpr int O_COL = kN + kN / 2;
   static constexpr int OB_STRIDE = D;
-  static constexpr int TMEM_COLS = kN + 2 * D <= 256 ? 256 : 512;
+  static constexpr int TMEM_COLS = 512;
 };
 
 // UMMA shared-memory descriptor, 128-byte swizzle (sm100 layout): start >> 4
@@ -87,6 +88,16 @@ __device__ __forceinline__ void umma(uint32_t tmem_d, uint64_t adesc, uint64_t b
       "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// The same with A read from TMEM (K-major, two 16-bit K elements per column).
+__device__ __forceinline__ void umma_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc,
+                                        uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
 
@@ -186,14 +197,14 @@ __global__ void __launch_bounds__(kThreadsP, 1)
   unsigned char *smem = reinterpret_cast<unsigned char *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L::BAR_OFF);
-  uint64_t *q_full = bars + 0, *q_empty = bars + 1;
+  uint64_t *q_full = bars + 24, *q_empty = bars + 26;  // per Q buffer
   // K and V tiles ride separate two-stage rings: a K stage frees as soon as
   // its QK^T is done, so the next K load starts a softmax earlier than a V's
   uint64_t *k_full = bars + 2, *k_empty = bars + 4, *v_full = bars + 20, *v_empty = bars + 22;
   uint64_t *s_full = bars + 6, *s_free = bars + 7, *p_full = bars + 8, *o_done = bars + 9;
   uint64_t *o_full = bars + 10, *o_free = bars + 12, *it_full = bars + 14, *it_empty = bars + 16;
   uint64_t *xch = bars + 18, *lxch = bars + 19;  // the two softmax halves' row max / row sum
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 24);
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 28);
   PfItem *items = reinterpret_cast<PfItem *>(smem + L::ITEM_OFF);
   int *tiles_pre = reinterpret_cast<int *>(smem + L::META_OFF);
   int *s_qo = tiles_pre + (kMaxBatchTc + 1);       // qo_indptr
@@ -227,8 +238,10 @@ __global__ void __launch_bounds__(kThreadsP, 1)
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      mbar_init(q_full, 1);
-      mbar_init(q_empty, 1);
+      for (int i = 0; i < 2; ++i) {
+        mbar_init(&q_full[i], 1);
+        mbar_init(&q_empty[i], 1);
+      }
       for (int i = 0; i < 2; ++i) {
         mbar_init(&k_full[i], 1);
         mbar_init(&k_empty[i], 1);
@@ -315,15 +328,16 @@ __global__ void __launch_bounds__(kThreadsP, 1)
       };
       int pw = load_win(0), pwn = load_win(1);
       // Q tile into the single Q buffer once the previous item's last QK^T is done
-      if (qc > 0 && !__all_sync(0xffffffffu, mbar_wait_bounded(q_empty, (qc - 1) & 1))) {
+      const int qb = qc & 1;  // Q buffer of this item
+      if (qc >= 2 && !__all_sync(0xffffffffu, mbar_wait_bounded(&q_empty[qb], ((qc >> 1) - 1) & 1))) {
         ok = false;
         break;
       }
       if (lane == 0) {
-        mbar_arrive_expect_tx(q_full, DH * m_used * 128);
+        mbar_arrive_expect_tx(&q_full[qb], DH * m_used * 128);
         for (int dh = 0; dh < DH; ++dh)
-          tma_load_3d(smem + L::Q_OFF + dh * kM * 128, &qmap, dh * 64, rec.h * g,
-                      rec.q_start + rec.t0, q_full, pol_q);
+          tma_load_3d(smem + L::Q_OFF + qb * L::Q_BYTES + dh * kM * 128, &qmap, dh * 64,
+                      rec.h * g, rec.q_start + rec.t0, &q_full[qb], pol_q);
       }
       ++qc;
       // K or V (which) of tile j of this item, global tile index gtile; page
@@ -376,7 +390,8 @@ __global__ void __launch_bounds__(kThreadsP, 1)
       if (ok && !issue(rec.n_tiles - 1, gt - 1, 1, pg_prev)) ok = false;
     }
     // no copy may be in flight when the CTA retires
-    if (qc > 0 && !__all_sync(0xffffffffu, mbar_wait_bounded(q_full, (qc - 1) & 1))) ok = false;
+    for (int t = max(0, qc - 2); t < qc; ++t)
+      if (!__all_sync(0xffffffffu, mbar_wait_bounded(&q_full[t & 1], (t >> 1) & 1))) ok = false;
     for (int t = max(0, gt - 2); t < gt; ++t)
       if (!__all_sync(0xffffffffu, mbar_wait_bounded(&k_full[t & 1], (t >> 1) & 1) &&
                                        mbar_wait_bounded(&v_full[t & 1], (t >> 1) & 1)))
@@ -387,9 +402,9 @@ __global__ void __launch_bounds__(kThreadsP, 1)
       const uint32_t fmt = std::is_same<T, __nv_bfloat16>::value ? 1u : 0u;
       const uint32_t idesc_qk = umma_idesc(fmt, false, kN, kM);
       const uint32_t idesc_pv = umma_idesc(fmt, true, D, kM);
-      const uint32_t q_addr = smem_u32(smem + L::Q_OFF);
-      const uint32_t p_addr = smem_u32(smem + L::P_OFF);
-      auto issue_qk = [&](int t) {  // S = Q K^T of global tile t (stage t & 1)
+      const uint32_t tmem_p = tmem + L::P_COL;
+      auto issue_qk = [&](int t, int qb) {  // S = Q K^T of global tile t (stage t & 1), Q buffer qb
+        const uint32_t q_addr = smem_u32(smem + L::Q_OFF + qb * L::Q_BYTES);
         const uint32_t k_addr = smem_u32(smem + L::KV_OFF + (t & 1) * L::STAGE_BYTES);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
@@ -418,17 +433,17 @@ __global__ void __launch_bounds__(kThreadsP, 1)
       PfItem cur, nxt;
       bool have = next_item(cur), have_next = false;
       if (have) {  // first QK^T
-        if (!mbar_wait_bounded(q_full, 0) || !mbar_wait_bounded(&k_full[0], 0)) ok = false;
+        if (!mbar_wait_bounded(&q_full[0], 0) || !mbar_wait_bounded(&k_full[0], 0)) ok = false;
         if (ok) {
           tc_fence_after();
-          issue_qk(0);
-          if (cur.n_tiles == 1) umma_commit(q_empty);
+          issue_qk(0, 0);
+          if (cur.n_tiles == 1) umma_commit(&q_empty[0]);
         }
       }
       int last_gt = -1;
       while (have && ok) {
         const int ob = oc & 1;
-        const uint32_t tmem_o = tmem + kN + ob * L::OB_STRIDE;
+        const uint32_t tmem_o = tmem + L::O_COL + ob * L::OB_STRIDE;
         for (int j = 0; j < cur.n_tiles && ok; ++j, ++gt) {
           // look ahead: QK^T of the next tile (this item's, or the next item's first)
           bool ahead = j + 1 < cur.n_tiles;
@@ -438,17 +453,18 @@ __global__ void __launch_bounds__(kThreadsP, 1)
             ahead = cross = have_next;
           }
           if (ahead) {
+            const int qn = cross ? qc + 1 : qc;  // the item the next tile belongs to
             if (!mbar_wait_bounded(s_free, gt & 1) ||
-                (cross && !mbar_wait_bounded(q_full, (qc + 1) & 1)) ||
+                (cross && !mbar_wait_bounded(&q_full[qn & 1], (qn >> 1) & 1)) ||
                 !mbar_wait_bounded(&k_full[(gt + 1) & 1], ((gt + 1) >> 1) & 1)) {
               ok = false;
               break;
             }
             tc_fence_after();
-            issue_qk(gt + 1);
-            // the last QK^T of its item frees the Q buffer for the item after
+            issue_qk(gt + 1, qn & 1);
+            // the last QK^T of its item frees its Q buffer for the item two later
             const bool last_qk = cross ? nxt.n_tiles == 1 : j + 2 == cur.n_tiles;
-            if (last_qk) umma_commit(q_empty);
+            if (last_qk) umma_commit(&q_empty[qn & 1]);
           }
           if (!mbar_wait_bounded(p_full, gt & 1) ||
               !mbar_wait_bounded(&v_full[gt & 1], (gt >> 1) & 1)) {
@@ -463,10 +479,10 @@ __global__ void __launch_bounds__(kThreadsP, 1)
           const uint32_t v_addr = smem_u32(smem + L::KV_OFF + (gt & 1) * L::STAGE_BYTES) + L::K_BYTES;
 #pragma unroll
           for (int kk = 0; kk < kN / 16; ++kk) {
-            const uint32_t aoff = (kk >> 2) * (kM * 128) + (kk & 3) * 32;
-            // V: MN-major, 64-wide d blocks kN*128 bytes apart, 8-token groups 1 KB apart
-            umma(tmem_o, umma_desc(p_addr + aoff, 16, 1024),
-                 umma_desc(v_addr + kk * 16 * 128, kN * 128, 1024), idesc_pv, (j > 0 || kk > 0));
+            // P from TMEM (16 keys = 8 columns per step); V: MN-major, 64-wide d
+            // blocks kN*128 bytes apart, 8-token groups 1 KB apart
+            umma_ts(tmem_o, tmem_p + kk * 8, umma_desc(v_addr + kk * 16 * 128, kN * 128, 1024),
+                    idesc_pv, (j > 0 || kk > 0));
           }
           umma_commit(&v_empty[gt & 1]);
           umma_commit(o_done);
@@ -496,7 +512,7 @@ __global__ void __launch_bounds__(kThreadsP, 1)
     const int r = qd * 32 + lane;  // packed row == TMEM lane
     const int t = r / g, jh = r % g;
     const uint32_t lane_base = static_cast<uint32_t>(qd * 32) << 16;
-    unsigned char *prow = smem + L::P_OFF;
+    const uint32_t tmem_p = tmem + L::P_COL + lane_base + sg * (SC / 2);  // this half's P columns
     float *xmax = reinterpret_cast<float *>(smem + L::XCH_OFF);  // [tile & 1][half][row]
     float *xsum = xmax + 4 * kM;                                  // [half][row]
     int gt = 0, oc = 0;
@@ -525,7 +541,7 @@ __global__ void __launch_bounds__(kThreadsP, 1)
       lim = min(lim, rec.lk);
       if (!row_ok) lim = 0;
       const int ob = oc & 1;
-      const uint32_t tmem_o = tmem + kN + ob * L::OB_STRIDE + sg * OC;
+      const uint32_t tmem_o = tmem + L::O_COL + ob * L::OB_STRIDE + sg * OC;
       float m = -INFINITY, l = 0.f;  // l: this half's share of the row sum
       for (int j = 0; j < rec.n_tiles; ++j, ++gt) {
         if (!__all_sync(0xffffffffu, mbar_wait_bounded(s_full, gt & 1))) { ok = false; break; }
@@ -570,15 +586,11 @@ __global__ void __launch_bounds__(kThreadsP, 1)
           if (!__all_sync(0xffffffffu, mbar_wait_bounded(o_done, (gt - 1) & 1))) { ok = false; break; }
           tc_fence_after();
         }
+        {  // P row: SC keys as 16-bit pairs into this half's TMEM columns
+          float pk[SC / 2];
 #pragma unroll
-        for (int cc = 0; cc < 8; ++cc) {
-          const float *x = sv + cc * 8;
-          uint4 w;
-          w.x = Pack2<T>::run(x[0], x[1]);
-          w.y = Pack2<T>::run(x[2], x[3]);
-          w.z = Pack2<T>::run(x[4], x[5]);
-          w.w = Pack2<T>::run(x[6], x[7]);
-          *reinterpret_cast<uint4 *>(prow + sg * (kM * 128) + swz(r, cc)) = w;
+          for (int c = 0; c < SC / 2; ++c) pk[c] = __uint_as_float(Pack2<T>::run(sv[2 * c], sv[2 * c + 1]));
+          tmem_st32(tmem_p, pk);
         }
         if (j > 0 && __any_sync(0xffffffffu, corr != 1.f)) {
 #pragma unroll
@@ -590,9 +602,8 @@ __global__ void __launch_bounds__(kThreadsP, 1)
             for (int i = 0; i < 32; ++i) ov[i] *= corr;
             tmem_st32(tmem_o + lane_base + c * 32, ov);
           }
-          tmem_wait_st();
         }
-        fence_proxy_async_smem();  // P visible to the tensor core
+        tmem_wait_st();  // P (and a rescaled O) are in TMEM before the MMA is told
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(p_full);
