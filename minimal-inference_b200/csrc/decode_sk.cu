@@ -61,13 +61,12 @@ struct SkParams {
   const void *q;
   int64_t qsb, qsh;
   int64_t num_pages;
-  int ps, hkv, group, hq, batch, subs, stages, stage_bytes, tps;
+  int ps, group, hq, batch, stages, stage_bytes, tps;  // KV heads: the kernel's HKV
   const int32_t *indptr, *indices, *last;
   float scale_log2;
   void *out;
   float *lse;
   int32_t *status;
-  unsigned *arrive;  // [batch * hkv] (reserved; the merge kernel needs no counters)
   float *part_o;     // [(grid + batch)][hq][D]
   float *part_lse;   // [(grid + batch)][hq]
   int bar_off, rec_off, scr_off;
@@ -704,11 +703,9 @@ int launch_decode_sk(const SkArgs &a) {
   p.qsh = a.qsh;
   p.num_pages = a.num_pages;
   p.ps = a.ps;
-  p.hkv = a.hkv;
   p.group = group;
   p.hq = a.hq;
   p.batch = a.batch;
-  p.subs = kNC / a.hkv;
   p.stages = L.stages;
   p.stage_bytes = L.stage_bytes;
   p.tps = L.tps;
@@ -719,7 +716,8 @@ int launch_decode_sk(const SkArgs &a) {
   p.out = a.out;
   p.lse = a.lse;
   p.status = a.status;
-  p.arrive = reinterpret_cast<unsigned *>(w + kCtrl);
+  // the workspace keeps decode.cu's layout: control, B*Hkv counters (used by
+  // the fallback kernel), then the partials
   p.part_o = reinterpret_cast<float *>(w + kCtrl + al256(size_t(a.batch) * a.hkv * 4));
   p.part_lse = reinterpret_cast<float *>(reinterpret_cast<unsigned char *>(p.part_o) +
                                          al256(slots * a.hq * a.d * 4));
