@@ -279,13 +279,19 @@ __global__ void __launch_bounds__(kThreadsP, 1)
     // ============================ producer ==================================
     const uint64_t pol_q = evict_last_policy(), pol_kv = evict_first_policy();
     int gt = 0, qc = 0;
+    int k_ahead = -1;  // lane 0: the next item's index, taken once this item's K tiles are out
     for (int it = 0; ok; ++it) {
       // next item: a counter shared by all CTAs (heaviest query tiles of each
       // request first), or round robin without a workspace
       // next item: a counter shared by all CTAs (heaviest query tiles of each
-      // request first), or round robin without a workspace
+      // request first), or round robin without a workspace; the counter is
+      // read while the previous item's last V tiles were being issued
       int k = 0;
-      if (lane == 0) k = p.ctr ? static_cast<int>(atomicAdd(p.ctr, 1u)) : blockIdx.x + it * gridDim.x;
+      if (lane == 0) {
+        k = k_ahead >= 0 ? k_ahead
+                         : (p.ctr ? static_cast<int>(atomicAdd(p.ctr, 1u)) : blockIdx.x + it * gridDim.x);
+        k_ahead = -1;
+      }
       k = __shfl_sync(0xffffffffu, k, 0);
       PfItem rec{-1, 0, 0, 0, 0, 0, 0, 0};
       if (k < n_items) {
@@ -384,7 +390,10 @@ __global__ void __launch_bounds__(kThreadsP, 1)
           pwn = load_win((j >> 2) + 1);
         }
         const int pg = __shfl_sync(0xffffffffu, pw, ((j & 3) << 3) + min(lane / DH, 7));
-        if (!issue(j, gt, 0, pg) || (j > 0 && !issue(j - 1, gt - 1, 1, pg_prev))) ok = false;
+        if (!issue(j, gt, 0, pg)) ok = false;
+        if (ok && j + 1 == rec.n_tiles && lane == 0 && p.ctr)
+          k_ahead = static_cast<int>(atomicAdd(p.ctr, 1u));  // used after the V tiles below
+        if (ok && j > 0 && !issue(j - 1, gt - 1, 1, pg_prev)) ok = false;
         pg_prev = pg;
       }
       if (ok && !issue(rec.n_tiles - 1, gt - 1, 1, pg_prev)) ok = false;
