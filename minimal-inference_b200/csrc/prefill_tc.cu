@@ -48,10 +48,12 @@ template <int D> struct PfLayout {
   static constexpr int Q_BYTES = DH * kM * 128;       // [dh][row][64]
   static constexpr int K_BYTES = DH * kN * 128;       // [dh][token][64]
   static constexpr int V_BYTES = K_BYTES;
-  static constexpr int STAGE_BYTES = K_BYTES + V_BYTES;
-  static constexpr int Q_OFF = 0;                      // two Q buffers (items alternate)
-  static constexpr int KV_OFF = Q_OFF + 2 * Q_BYTES;
-  static constexpr int BAR_OFF = KV_OFF + 2 * STAGE_BYTES;  // 28 mbarriers + tmem base
+  // ring depths: Q buffers (items), K stages, V stages (tiles)
+  static constexpr int NQ = 2, NK = 2, NV = 2;
+  static constexpr int Q_OFF = 0;
+  static constexpr int K_OFF = Q_OFF + NQ * Q_BYTES;
+  static constexpr int V_OFF = K_OFF + NK * K_BYTES;
+  static constexpr int BAR_OFF = V_OFF + NV * V_BYTES;  // 28 mbarriers + tmem base
   static constexpr int ITEM_OFF = BAR_OFF + 256;       // 2 work-item records
   static constexpr int XCH_OFF = ITEM_OFF + 64;        // row max [2 tiles][2 halves][128], row sum [2][128]
   static constexpr int META_OFF = XCH_OFF + (2 * 2 * kM + 2 * kM) * 4;
@@ -197,13 +199,13 @@ __global__ void __launch_bounds__(kThreadsP, 1)
   unsigned char *smem = reinterpret_cast<unsigned char *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L::BAR_OFF);
-  uint64_t *q_full = bars + 24, *q_empty = bars + 26;  // per Q buffer
-  // K and V tiles ride separate two-stage rings: a K stage frees as soon as
-  // its QK^T is done, so the next K load starts a softmax earlier than a V's
-  uint64_t *k_full = bars + 2, *k_empty = bars + 4, *v_full = bars + 20, *v_empty = bars + 22;
-  uint64_t *s_full = bars + 6, *s_free = bars + 7, *p_full = bars + 8, *o_done = bars + 9;
-  uint64_t *o_full = bars + 10, *o_free = bars + 12, *it_full = bars + 14, *it_empty = bars + 16;
-  uint64_t *xch = bars + 18, *lxch = bars + 19;  // the two softmax halves' row max / row sum
+  uint64_t *q_full = bars + 0, *q_empty = bars + 2;  // per Q buffer (NQ <= 2)
+  // K and V tiles ride separate rings: a K stage frees as soon as its QK^T is
+  // done, so K loads run ahead of V loads (NK <= 3, NV <= 2)
+  uint64_t *k_full = bars + 4, *k_empty = bars + 7, *v_full = bars + 10, *v_empty = bars + 12;
+  uint64_t *s_full = bars + 14, *s_free = bars + 15, *p_full = bars + 16, *o_done = bars + 17;
+  uint64_t *o_full = bars + 18, *o_free = bars + 20, *it_full = bars + 22, *it_empty = bars + 24;
+  uint64_t *xch = bars + 26, *lxch = bars + 27;  // the two softmax halves' row max / row sum
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 28);
   PfItem *items = reinterpret_cast<PfItem *>(smem + L::ITEM_OFF);
   int *tiles_pre = reinterpret_cast<int *>(smem + L::META_OFF);
@@ -238,15 +240,19 @@ __global__ void __launch_bounds__(kThreadsP, 1)
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      for (int i = 0; i < 2; ++i) {
+      for (int i = 0; i < L::NQ; ++i) {
         mbar_init(&q_full[i], 1);
         mbar_init(&q_empty[i], 1);
       }
-      for (int i = 0; i < 2; ++i) {
+      for (int i = 0; i < L::NK; ++i) {
         mbar_init(&k_full[i], 1);
         mbar_init(&k_empty[i], 1);
+      }
+      for (int i = 0; i < L::NV; ++i) {
         mbar_init(&v_full[i], 1);
         mbar_init(&v_empty[i], 1);
+      }
+      for (int i = 0; i < 2; ++i) {
         mbar_init(&o_full[i], 1);
         mbar_init(&o_free[i], 8);
         mbar_init(&it_full[i], 1);
@@ -334,8 +340,9 @@ __global__ void __launch_bounds__(kThreadsP, 1)
       };
       int pw = load_win(0), pwn = load_win(1);
       // Q tile into the single Q buffer once the previous item's last QK^T is done
-      const int qb = qc & 1;  // Q buffer of this item
-      if (qc >= 2 && !__all_sync(0xffffffffu, mbar_wait_bounded(&q_empty[qb], ((qc >> 1) - 1) & 1))) {
+      const int qb = qc % L::NQ;  // Q buffer of this item
+      if (qc >= L::NQ &&
+          !__all_sync(0xffffffffu, mbar_wait_bounded(&q_empty[qb], ((qc / L::NQ) - 1) & 1))) {
         ok = false;
         break;
       }
@@ -349,16 +356,17 @@ __global__ void __launch_bounds__(kThreadsP, 1)
       // K or V (which) of tile j of this item, global tile index gtile; page
       // is this lane's chunk's page id (chunk lane / DH of the tile)
       auto issue = [&](int j, int gtile, int which, int page) -> bool {
-        const int st = gtile & 1;
+        const int nst = which ? L::NV : L::NK;
+        const int st = gtile % nst;
         uint64_t *full = which ? &v_full[st] : &k_full[st];
         uint64_t *empty = which ? &v_empty[st] : &k_empty[st];
-        if (gtile >= 2 &&
-            !__all_sync(0xffffffffu, mbar_wait_bounded(empty, ((gtile >> 1) - 1) & 1)))
+        if (gtile >= nst &&
+            !__all_sync(0xffffffffu, mbar_wait_bounded(empty, ((gtile / nst) - 1) & 1)))
           return false;
         const int tok_tile = j * kN;
         const int nvc = min(8, cdiv(rec.lk - tok_tile, 16));
-        unsigned char *base = smem + L::KV_OFF + st * L::STAGE_BYTES + which * L::K_BYTES;
-        if (which == 1 && gtile < 2 && nvc < 8) {
+        unsigned char *base = smem + (which ? L::V_OFF + st * L::V_BYTES : L::K_OFF + st * L::K_BYTES);
+        if (which == 1 && gtile < L::NV && nvc < 8) {
           // V chunks past the request's end are multiplied by P = 0; on a
           // stage's first use they hold whatever shared memory held, so zero
           // them (later uses keep an earlier tile's finite values there)
@@ -399,11 +407,14 @@ __global__ void __launch_bounds__(kThreadsP, 1)
       if (ok && !issue(rec.n_tiles - 1, gt - 1, 1, pg_prev)) ok = false;
     }
     // no copy may be in flight when the CTA retires
-    for (int t = max(0, qc - 2); t < qc; ++t)
-      if (!__all_sync(0xffffffffu, mbar_wait_bounded(&q_full[t & 1], (t >> 1) & 1))) ok = false;
-    for (int t = max(0, gt - 2); t < gt; ++t)
-      if (!__all_sync(0xffffffffu, mbar_wait_bounded(&k_full[t & 1], (t >> 1) & 1) &&
-                                       mbar_wait_bounded(&v_full[t & 1], (t >> 1) & 1)))
+    for (int t = max(0, qc - L::NQ); t < qc; ++t)
+      if (!__all_sync(0xffffffffu, mbar_wait_bounded(&q_full[t % L::NQ], (t / L::NQ) & 1)))
+        ok = false;
+    for (int t = max(0, gt - L::NK); t < gt; ++t)
+      if (!__all_sync(0xffffffffu, mbar_wait_bounded(&k_full[t % L::NK], (t / L::NK) & 1)))
+        ok = false;
+    for (int t = max(0, gt - L::NV); t < gt; ++t)
+      if (!__all_sync(0xffffffffu, mbar_wait_bounded(&v_full[t % L::NV], (t / L::NV) & 1)))
         ok = false;
   } else if (warp == 1) {
     // ============================ MMA issuer ================================
@@ -414,7 +425,7 @@ __global__ void __launch_bounds__(kThreadsP, 1)
       const uint32_t tmem_p = tmem + L::P_COL;
       auto issue_qk = [&](int t, int qb) {  // S = Q K^T of global tile t (stage t & 1), Q buffer qb
         const uint32_t q_addr = smem_u32(smem + L::Q_OFF + qb * L::Q_BYTES);
-        const uint32_t k_addr = smem_u32(smem + L::KV_OFF + (t & 1) * L::STAGE_BYTES);
+        const uint32_t k_addr = smem_u32(smem + L::K_OFF + (t % L::NK) * L::K_BYTES);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t off = (kk >> 2) * (kM * 128) + (kk & 3) * 32;
@@ -423,7 +434,7 @@ __global__ void __launch_bounds__(kThreadsP, 1)
                idesc_qk, kk > 0);
         }
         umma_commit(s_full);
-        umma_commit(&k_empty[t & 1]);
+        umma_commit(&k_empty[t % L::NK]);
       };
       // Items come in order; the next item with keys is looked up ahead so
       // its first QK^T can run under the softmax of this item's last tile.
@@ -464,19 +475,19 @@ __global__ void __launch_bounds__(kThreadsP, 1)
           if (ahead) {
             const int qn = cross ? qc + 1 : qc;  // the item the next tile belongs to
             if (!mbar_wait_bounded(s_free, gt & 1) ||
-                (cross && !mbar_wait_bounded(&q_full[qn & 1], (qn >> 1) & 1)) ||
-                !mbar_wait_bounded(&k_full[(gt + 1) & 1], ((gt + 1) >> 1) & 1)) {
+                (cross && !mbar_wait_bounded(&q_full[qn % L::NQ], (qn / L::NQ) & 1)) ||
+                !mbar_wait_bounded(&k_full[(gt + 1) % L::NK], ((gt + 1) / L::NK) & 1)) {
               ok = false;
               break;
             }
             tc_fence_after();
-            issue_qk(gt + 1, qn & 1);
-            // the last QK^T of its item frees its Q buffer for the item two later
+            issue_qk(gt + 1, qn % L::NQ);
+            // the last QK^T of its item frees its Q buffer for a later item
             const bool last_qk = cross ? nxt.n_tiles == 1 : j + 2 == cur.n_tiles;
-            if (last_qk) umma_commit(&q_empty[qn & 1]);
+            if (last_qk) umma_commit(&q_empty[qn % L::NQ]);
           }
           if (!mbar_wait_bounded(p_full, gt & 1) ||
-              !mbar_wait_bounded(&v_full[gt & 1], (gt >> 1) & 1)) {
+              !mbar_wait_bounded(&v_full[gt % L::NV], (gt / L::NV) & 1)) {
             ok = false;
             break;
           }
@@ -485,7 +496,7 @@ __global__ void __launch_bounds__(kThreadsP, 1)
             break;
           }
           tc_fence_after();
-          const uint32_t v_addr = smem_u32(smem + L::KV_OFF + (gt & 1) * L::STAGE_BYTES) + L::K_BYTES;
+          const uint32_t v_addr = smem_u32(smem + L::V_OFF + (gt % L::NV) * L::V_BYTES);
 #pragma unroll
           for (int kk = 0; kk < kN / 16; ++kk) {
             // P from TMEM (16 keys = 8 columns per step); V: MN-major, 64-wide d
@@ -493,7 +504,7 @@ __global__ void __launch_bounds__(kThreadsP, 1)
             umma_ts(tmem_o, tmem_p + kk * 8, umma_desc(v_addr + kk * 16 * 128, kN * 128, 1024),
                     idesc_pv, (j > 0 || kk > 0));
           }
-          umma_commit(&v_empty[gt & 1]);
+          umma_commit(&v_empty[gt % L::NV]);
           umma_commit(o_done);
           if (j + 1 == cur.n_tiles) umma_commit(&o_full[ob]);
           last_gt = gt;
@@ -563,13 +574,18 @@ __global__ void __launch_bounds__(kThreadsP, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(s_free);
+        // raw scores; the scale is folded into the exponent's FMA below.
+        // Keys past a row's limit count as -inf; only warps with such a row
+        // in this tile pay for the mask.
         const int kbase = j * kN + sg * SC;
+        if (__any_sync(0xffffffffu, kbase + SC > lim)) {
+#pragma unroll
+          for (int c = 0; c < SC; ++c) sv[c] = (kbase + c < lim) ? sv[c] : -INFINITY;
+        }
         float mt = -INFINITY;
 #pragma unroll
-        for (int c = 0; c < SC; ++c) {
-          sv[c] = (kbase + c < lim) ? sv[c] * p.scale_log2 : -INFINITY;
-          mt = fmaxf(mt, sv[c]);
-        }
+        for (int c = 0; c < SC; ++c) mt = fmaxf(mt, sv[c]);
+        mt *= p.scale_log2;  // scale_log2 > 0: the max commutes with it
         // row max over both halves
         float *xm = xmax + (gt & 1) * 2 * kM;
         xm[sg * kM + r] = mt;
@@ -585,7 +601,7 @@ __global__ void __launch_bounds__(kThreadsP, 1)
         float sum = 0.f;
 #pragma unroll
         for (int c = 0; c < SC; ++c) {
-          sv[c] = fast_exp2(sv[c] - ms);
+          sv[c] = fast_exp2(fmaf(sv[c], p.scale_log2, -ms));
           sum += sv[c];
         }
         l = l * corr + sum;
@@ -711,6 +727,7 @@ int launch_prefill_tc(const PrefillParams &p, int dtype, cudaStream_t s) {
   if (!(p.d == 64 || p.d == 128)) return -1;
   if (p.group > kM || p.ps % 16 != 0 || p.ps > 256 || p.batch > kMaxBatchTc) return -1;
   if (p.hkv > 65535 || p.num_pages * 2 > (1LL << 31)) return -1;
+  if (!(p.scale_log2 > 0.f)) return -1;  // the softmax takes the row max before scaling
   if (static_cast<int64_t>(p.total_q) + kM > (1LL << 31)) return -1;
   if (dtype == MI_DTYPE_BF16)
     return p.d == 128 ? launch_t<__nv_bfloat16, 128>(p, dtype, s)
