@@ -592,15 +592,9 @@ size_t fast_ws_bytes(int batch, int hq, int hkv, int d, int max_items) {
 template <typename T, int D, bool G16>
 int launch_tc(DecodeParams p, void *ws, size_t ws_bytes, cudaStream_t s) {
   using L = TcLayout<D>;
-  static unsigned long long attr_set = 0;  // one bit per device
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (!(attr_set >> (dev & 63) & 1ull)) {
-    if (cudaFuncSetAttribute(decode_tc_kernel<T, D, G16>,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize, L::SMEM) != cudaSuccess)
-      return check_launch("decode_tc_kernel smem attribute");
-    attr_set |= 1ull << (dev & 63);
-  }
+  static std::atomic<unsigned long long> attr_set{0};
+  if (smem_limit_once(attr_set, decode_tc_kernel<T, D, G16>, L::SMEM) != cudaSuccess)
+    return check_launch("decode_tc_kernel smem attribute");
   const int group = p.hq / p.hkv;
   unsigned char *w = static_cast<unsigned char *>(ws);
   p.ctrl = reinterpret_cast<unsigned int *>(w);

@@ -637,16 +637,9 @@ bool sk_layout(int hkv, int d, int group, int batch, SkLayout *L) {
 template <typename T, int D, bool G16, int HKV>
 int launch_sk_t(const SkArgs &a, const CUtensorMap &map, const SkParams &p, int grid,
                 int smem) {
-  static unsigned long long attr_set = 0;
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (!(attr_set >> (dev & 63) & 1ull)) {
-    if (cudaFuncSetAttribute(decode_sk_kernel<T, D, G16, HKV>,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             kSmemLimit) != cudaSuccess)
-      return check_launch("decode_sk_kernel smem attribute");
-    attr_set |= 1ull << (dev & 63);
-  }
+  static std::atomic<unsigned long long> attr_set{0};
+  if (smem_limit_once(attr_set, decode_sk_kernel<T, D, G16, HKV>, kSmemLimit) != cudaSuccess)
+    return check_launch("decode_sk_kernel smem attribute");
   cudaError_t e = launch_pdl(decode_sk_kernel<T, D, G16, HKV>, dim3(grid), dim3(kThreads), smem,
                              a.stream, map, p);
   if (e != cudaSuccess) return fail(MI_ERR_CUDA, "decode_sk_kernel launch: %s", cudaGetErrorString(e));

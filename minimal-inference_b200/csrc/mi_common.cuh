@@ -6,6 +6,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
 #include <utility>
 
 #include "../../include/mi_paged.h"
@@ -19,6 +20,21 @@ void set_error(const char *fmt, ...);
 int fail(int code, const char *fmt, ...);
 int check_launch(const char *what);
 int num_sms();
+
+// Raise `kernel`'s dynamic shared-memory limit to `bytes` once per device
+// (`done` keeps one bit per device; safe when several host threads launch).
+// Setting the attribute twice is harmless, so racing first calls need no lock.
+template <typename K>
+cudaError_t smem_limit_once(std::atomic<unsigned long long> &done, K kernel, int bytes) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  const unsigned long long bit = 1ull << (dev & 63);
+  if (done.load(std::memory_order_acquire) & bit) return cudaSuccess;
+  e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess) done.fetch_or(bit, std::memory_order_release);
+  return e;
+}
 
 #define MI_REQUIRE(cond, ...)                           \
   do {                                                  \

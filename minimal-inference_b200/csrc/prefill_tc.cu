@@ -703,15 +703,9 @@ int launch_t(const PrefillParams &p, int dtype, cudaStream_t s) {
   if (!rows_tensor_map(p.q, p.total_q, p.hq, D, p.qsn, p.qsh, p.group, tq, dtype, &qmap))
     return -1;
   if (!pool_tensor_map(p.kv, p.num_pages, p.ps, p.hkv, D, dtype, &kvmap)) return -1;
-  static unsigned long long attr_set = 0;
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (!(attr_set >> (dev & 63) & 1ull)) {
-    if (cudaFuncSetAttribute(prefill_tc_kernel<T, D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             L::SMEM) != cudaSuccess)
-      return check_launch("prefill_tc_kernel smem attribute");
-    attr_set |= 1ull << (dev & 63);
-  }
+  static std::atomic<unsigned long long> attr_set{0};
+  if (smem_limit_once(attr_set, prefill_tc_kernel<T, D>, L::SMEM) != cudaSuccess)
+    return check_launch("prefill_tc_kernel smem attribute");
   // persistent: one CTA per SM, or fewer when there are fewer work items
   // (an upper bound on the items: (sum ceil(L_b / tq)) * hkv <= (total/tq + batch) * hkv)
   const int64_t items = (static_cast<int64_t>(p.total_q) / tq + p.batch) * p.hkv;
