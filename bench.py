@@ -219,6 +219,10 @@ def model_decode(dev, batch=32, out_tokens=50, seed=3):
            "value": round(batch / (t2t_ms / 1e3), 1), "unit": "tok/s",
            "t2t_ms": round(t2t_ms, 3),
            "decode_step_ms_median": round(statistics.median(decode_steps), 3),
+           "decode_step_ms_mean": round(statistics.mean(decode_steps), 3),
+           "decode_step_ms_p90_max": [round(float(np.percentile(decode_steps, 90)), 3),
+                                      round(max(decode_steps), 3)],
+           "decode_step_ms_first5": [round(x, 3) for x in decode_steps[:5]],
            "first_step_ms (prefill of all 32 + 1 decode)": round(step_ms[0], 2),
            "wall_s": round(total_s, 3), "batch": batch, "output_tokens": out_tokens,
            "prompt_lens": "U[128,1024] seeded", "weights": "random N(0,0.02) bf16",
