@@ -449,6 +449,9 @@ DECODE_SHAPES = [  # (batch, Q heads, KV heads, ctx lo, ctx hi, note)
     (64, 16, 2, 512, 4096, "Qwen2.5-72B at TP 4"),
     (64, 8, 1, 512, 4096, "Qwen2.5-72B at TP 8"),
     (32, 28, 4, 256, 4096, "Qwen2.5-7B (group 7)"),
+    (32, 16, 4, 256, 4096, "config 2 head-sharded over 2 GPUs: one GPU's heads"),
+    (32, 8, 2, 256, 4096, "config 2 head-sharded over 4 GPUs: one GPU's heads"),
+    (32, 4, 1, 256, 4096, "config 2 head-sharded over 8 GPUs: one GPU's heads"),
 ]
 
 

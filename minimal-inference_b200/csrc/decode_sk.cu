@@ -23,8 +23,11 @@
 //     (the next window is prefetched). For each stage it waits for a free
 //     slot, writes the stage record, and its lanes issue one 4-D TMA tensor
 //     load (cp.async.bulk.tensor, SWIZZLE_128B) per (tile, K/V, 64-wide half
-//     of head_dim, KV head): a 16-token x 128-byte box. The stage's mbarrier
-//     counts the bytes.
+//     of head_dim): a 16-token x Hkv-head x 128-byte box, laid out in shared
+//     memory as [head][token][128 bytes] (with one KV head, one 5-D box per
+//     tile). The stage's mbarrier counts the bytes. Whole-head boxes matter:
+//     with one box per head the TMA issue rate, not HBM, bounded the kernel
+//     (config 2: 60.7 us per launch with 32 boxes per tile, 52.9 with 4).
 //   * Consumers: warp w serves KV head w / (8/Hkv); the 8/Hkv warps of a
 //     head take turns over the tiles of a segment, one tile per stage at
 //     most. The group's query heads are the M
@@ -90,7 +93,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr int SUBS = kNC / HKV;                         // consumer warps per KV head
   constexpr int kBlockBytes = HKV * kTile * 128;          // one (K/V, d-half) block of a tile
   constexpr int kTileBytes = 2 * DH * kBlockBytes;        // one 16-token tile of all heads
-  constexpr int kBoxes = 2 * DH * HKV;                    // TMA boxes per tile
+  // TMA boxes per tile: one per (K/V, d-half) covering all heads, or with a
+  // single KV head one box for the whole tile (measured faster there, and
+  // slower at 2 and 4 heads)
+  constexpr bool kWholeTile = HKV == 1;
+  constexpr int kBoxes = kWholeTile ? 1 : 2 * DH;
   extern __shared__ unsigned char smem_raw[];
   unsigned char *smem = reinterpret_cast<unsigned char *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -181,7 +188,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         // A segment without tokens (last_page_len 0) still gets one fully
         // masked tile, so its partial and its merge arrival exist.
         const int ntiles = tok_end > tok_begin ? cdiv(tok_end - tok_begin, kTile) : 1;
-        constexpr int nbox = kBoxes;  // nbox * tps <= 32
         for (int j0 = 0, ord = 0; j0 < ntiles; j0 += p.tps, ++ord) {
           const int nt = min(p.tps, ntiles - j0);
           const int tok0 = tok_begin + j0 * kTile;
@@ -191,16 +197,16 @@ __global__ void __launch_bounds__(kThreads, 1)
             pw = pwn;
             pwn = (wbase + 32 + lane < total) ? p.indices[base0 + wbase + 32 + lane] : -1;
           }
-          // lane -> (tile t, K/V, d-half, head); a stage spans at most 9 pages,
+          // lane -> (tile t, K/V, d-half); a stage spans at most 9 pages,
           // so its page ids sit in the current or the next window
-          const int t = lane / nbox, r = lane % nbox;
+          const int t = lane / kBoxes, r = lane % kBoxes;
           const int ttok = tok0 + t * kTile;
           int page;
           bool mine, bad;
           int badmask = 0;
           if constexpr (SUBS == 1) {  // one tile per stage, one page id for all lanes
             page = __shfl_sync(0xffffffffu, pw, gpos0 - wbase);
-            mine = true;
+            mine = t < nt;
             bad = page < 0 || page >= p.num_pages;
             badmask = bad ? 1 : 0;
           } else {
@@ -211,17 +217,16 @@ __global__ void __launch_bounds__(kThreads, 1)
             mine = t < nt;
             bad = mine && (page < 0 || page >= p.num_pages);
             const unsigned badl = __ballot_sync(0xffffffffu, bad);
-            for (int tt = 0; tt < nt; ++tt) badmask |= ((badl >> (tt * nbox)) & 1u) << tt;
+            for (int tt = 0; tt < nt; ++tt) badmask |= ((badl >> (tt * kBoxes)) & 1u) << tt;
           }
           // everything but the issue itself is ready before the wait for a free slot
           const int s = k % S;
           const int flags = (j0 == 0 ? 1 : 0) | (j0 + nt >= ntiles ? 2 : 0) | (direct ? 4 : 0) |
                             (badmask << 8) | (nt << 16) | ((ord & 2047) << 20);
           const uint32_t tx = static_cast<uint32_t>(nt - __popc(badmask)) * kTileBytes;
-          const int h = r % HKV, rest = r / HKV;
-          const int dh = rest % DH, which = rest / DH;
-          unsigned char *dst = smem + s * p.stage_bytes + t * kTileBytes +
-                               (which * DH + dh) * block_bytes + h * (kTile * 128);
+          const int dh = r % DH, which = r / DH;
+          unsigned char *dst =
+              smem + s * p.stage_bytes + t * kTileBytes + (which * DH + dh) * block_bytes;
           const int row = ttok % p.ps, plane = page * 2 + which;
           if (!__all_sync(0xffffffffu, mbar_wait_bounded(&empty[s], ((k / S) & 1) ^ 1))) {
             ok_run = false;
@@ -233,7 +238,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (badmask) flag(p.status, MI_STATUS_BAD_PAGE);
           }
           __syncwarp();
-          if (mine && !bad) tma_load_4d(dst, &tmap, dh * 64, h, row, plane, &full[s], policy);
+          if (mine && !bad) {
+            if constexpr (kWholeTile)
+              tma_load_5d(dst, &tmap, 0, row, 0, 0, plane, &full[s], policy);
+            else
+              tma_load_4d(dst, &tmap, dh * 64, row, 0, plane, &full[s], policy);
+          }
           ++k;
         }
         pos = sub_hi;
@@ -686,7 +696,10 @@ int launch_decode_sk(const SkArgs &a) {
   SkLayout L;
   if (!sk_layout(a.hkv, a.d, group, a.batch, &L)) return -1;
   CUtensorMap map;
-  if (!pool_tensor_map(a.kv, a.num_pages, a.ps, a.hkv, a.d, a.dtype, &map)) return -1;
+  const bool mapped = a.hkv == 1
+                          ? pool_tile_tensor_map(a.kv, a.num_pages, a.ps, a.hkv, a.d, a.dtype, &map)
+                          : pool_tensor_map(a.kv, a.num_pages, a.ps, a.hkv, a.d, a.dtype, &map, true);
+  if (!mapped) return -1;
   const int grid = num_sms();
   unsigned char *w = static_cast<unsigned char *>(a.ws);
   const size_t slots = static_cast<size_t>(grid) + a.batch;
