@@ -890,7 +890,9 @@ def main():
         torch.cuda.current_stream(dev).wait_stream(side)
         torch.cuda.synchronize()
         graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph):
+        # thread-local capture: the process group's watchdog thread may query
+        # its CUDA events while this thread captures
+        with torch.cuda.graph(graph, capture_error_mode="thread_local"):
             e2e_step()
         for _ in range(3):
             graph.replay()
