@@ -10,7 +10,7 @@
 // is persistent, one CTA per SM; CTAs take items from a counter shared
 // through the workspace (each request's heaviest query tiles first), so set-up
 // (barriers, TMEM, the query-tile prefix) is paid once per SM and the next
-// item's metadata, Q and K/V loads run under the current item. Six warps:
+// item's metadata, Q and K/V loads run under the current item. 14 warps:
 //   warp 0  producer: TMA loads of the Q tile (3-D map over q) and of 128-token
 //           K/V tiles straight from the pages (4-D pool map, 16-token boxes),
 //           two K/V stages, 128-byte swizzle;
@@ -20,14 +20,16 @@
 //           mbarriers. S of tile j+1 is issued as soon as the softmax warps
 //           hold S of tile j in registers, so it runs under their softmax;
 //           P V of tile j follows once P is written;
-//   warps 2-9  softmax and epilogue, two halves of four warps (S columns and
-//           O columns split between them): thread = TMEM lane = query row. Each KV
+//   warps 2-9  softmax, two halves of four warps (S columns and O columns
+//           split between them): thread = TMEM lane = query row. Each KV
 //           tile: load the S row, causal/length mask, online softmax in the
-//           exp2 domain, write the bf16 P row into a 128-byte-swizzled tile,
-//           rescale the O row in TMEM only when the row max grew by more
-//           than 2^8; at the end normalise O and store it.
-// TMEM: S in columns [0,128), two O buffers (items alternate, so one item's
-// first products go in while the previous item's epilogue reads). Every wait
+//           exp2 domain, write the bf16 P row into TMEM, rescale the O row in
+//           TMEM only when the row max grew by more than 2^8; at the item's
+//           end hand the row sums to the epilogue warps and go on;
+//   warps 10-13 epilogue: normalise the finished item's O and store it while
+//           the softmax warps work on the next item.
+// TMEM: S in columns [0,128), P, two O buffers (items alternate, so one
+// item's first products go in while the epilogue reads the previous one's O). Every wait
 // is bounded; TMEM is freed on every path.
 #include <algorithm>
 #include <type_traits>
@@ -40,7 +42,7 @@ namespace {
 
 constexpr int kM = 128;       // packed query rows per CTA
 constexpr int kN = 128;       // KV tokens per tile
-constexpr int kThreadsP = 320;  // producer, MMA issuer, 2 x 4 softmax warps
+constexpr int kThreadsP = 448;  // producer, MMA issuer, 2 x 4 softmax warps, 4 epilogue warps
 constexpr int kMaxBatchTc = 1024;
 
 template <int D> struct PfLayout {
@@ -53,10 +55,15 @@ template <int D> struct PfLayout {
   static constexpr int Q_OFF = 0;
   static constexpr int K_OFF = Q_OFF + NQ * Q_BYTES;
   static constexpr int V_OFF = K_OFF + NK * K_BYTES;
-  static constexpr int BAR_OFF = V_OFF + NV * V_BYTES;  // 28 mbarriers + tmem base
+  static constexpr int BAR_OFF = V_OFF + NV * V_BYTES;  // 31 mbarriers + tmem base
   static constexpr int ITEM_OFF = BAR_OFF + 256;       // 2 work-item records
-  static constexpr int XCH_OFF = ITEM_OFF + 64;        // row max [2 tiles][2 halves][128], row sum [2][128]
-  static constexpr int META_OFF = XCH_OFF + (2 * 2 * kM + 2 * kM) * 4;
+  // row max exchange [2 tiles][2 halves][128]; per O buffer: row sums
+  // [2][2 halves][128], row max [2][128] and the item's output record
+  static constexpr int XCH_OFF = ITEM_OFF + 64;
+  static constexpr int LSUM_OFF = XCH_OFF + 2 * 2 * kM * 4;
+  static constexpr int MFIN_OFF = LSUM_OFF + 2 * 2 * kM * 4;
+  static constexpr int EREC_OFF = MFIN_OFF + 2 * kM * 4;
+  static constexpr int META_OFF = EREC_OFF + 2 * 16;
   // tiles_pre, qo_indptr, kv_indptr [batch+1] and kv_len [batch], in shared memory
   static constexpr int META_INTS = 4 * (kMaxBatchTc + 1);
   static constexpr int SMEM = META_OFF + META_INTS * 4 + 1024;
@@ -190,6 +197,8 @@ struct __align__(16) PfItem {
 };
 
 template <typename T, int D>
+// 14 warps: four of them share one SM sub-partition's 16 K registers, so at
+// most 128 registers per thread
 __global__ void __launch_bounds__(kThreadsP, 1)
     prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap,
                       const __grid_constant__ CUtensorMap kvmap, const PrefillParams p) {
@@ -205,8 +214,9 @@ __global__ void __launch_bounds__(kThreadsP, 1)
   uint64_t *k_full = bars + 4, *k_empty = bars + 7, *v_full = bars + 10, *v_empty = bars + 12;
   uint64_t *s_full = bars + 14, *s_free = bars + 15, *p_full = bars + 16, *o_done = bars + 17;
   uint64_t *o_full = bars + 18, *o_free = bars + 20, *it_full = bars + 22, *it_empty = bars + 24;
-  uint64_t *xch = bars + 26, *lxch = bars + 27;  // the two softmax halves' row max / row sum
+  uint64_t *xch = bars + 26;  // the two softmax halves' row maxima
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 28);
+  uint64_t *l_ready = bars + 29;  // per O buffer: the item's row sums are in shared memory
   PfItem *items = reinterpret_cast<PfItem *>(smem + L::ITEM_OFF);
   int *tiles_pre = reinterpret_cast<int *>(smem + L::META_OFF);
   int *s_qo = tiles_pre + (kMaxBatchTc + 1);       // qo_indptr
@@ -254,7 +264,8 @@ __global__ void __launch_bounds__(kThreadsP, 1)
       }
       for (int i = 0; i < 2; ++i) {
         mbar_init(&o_full[i], 1);
-        mbar_init(&o_free[i], 8);
+        mbar_init(&o_free[i], 4);   // the 4 epilogue warps
+        mbar_init(&l_ready[i], 8);  // the 8 softmax warps
         mbar_init(&it_full[i], 1);
         mbar_init(&it_empty[i], 9);  // the MMA thread and the 8 softmax warps
       }
@@ -263,7 +274,6 @@ __global__ void __launch_bounds__(kThreadsP, 1)
       mbar_init(p_full, 8);
       mbar_init(o_done, 1);
       mbar_init(xch, 8);
-      mbar_init(lxch, 8);
     }
     __syncwarp();
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
@@ -519,13 +529,15 @@ __global__ void __launch_bounds__(kThreadsP, 1)
       if (last_gt >= 0 && !mbar_wait_bounded(o_done, last_gt & 1)) ok = false;
     }
     __syncwarp();
-  } else {
-    // ================ softmax + epilogue (warps 2..9) ========================
+  } else if (warp < 10) {
+    // ======================== softmax (warps 2..9) ===========================
     // Two halves of four warps each: the half sg owns S columns
     // [64 sg, 64 sg + 64) (and so the P block sg) and O columns
     // [D/2 sg, D/2 sg + D/2); thread = TMEM lane = packed query row in both.
-    // Per tile the halves swap their row maxima (xch), per item their row
-    // sums (lxch), through shared memory behind bounded mbarrier waits.
+    // Per tile the halves swap their row maxima (xch) through shared memory
+    // behind a bounded mbarrier wait. At an item's end they leave its row
+    // sums, row max and output record for the epilogue warps (l_ready) and go
+    // on with the next item while O is read out.
     constexpr int SC = kN / 2, OC = D / 2;
     const int sg = (warp - 2) >> 2;
     const int qd = warp & 3;
@@ -534,8 +546,23 @@ __global__ void __launch_bounds__(kThreadsP, 1)
     const uint32_t lane_base = static_cast<uint32_t>(qd * 32) << 16;
     const uint32_t tmem_p = tmem + L::P_COL + lane_base + sg * (SC / 2);  // this half's P columns
     float *xmax = reinterpret_cast<float *>(smem + L::XCH_OFF);  // [tile & 1][half][row]
-    float *xsum = xmax + 4 * kM;                                  // [half][row]
+    float *lsum = reinterpret_cast<float *>(smem + L::LSUM_OFF);  // [ob][half][row]
+    float *mfin = reinterpret_cast<float *>(smem + L::MFIN_OFF);  // [ob][row]
+    int4 *erec = reinterpret_cast<int4 *>(smem + L::EREC_OFF);    // [ob]
     int gt = 0, oc = 0;
+    // hand buffer ob's record to the epilogue warps once they have finished
+    // with that buffer's previous item (its o_free)
+    auto hand_off = [&](int ob, int4 er, float l, float m) -> bool {
+      if (oc >= 2 &&
+          !__all_sync(0xffffffffu, mbar_wait_bounded(&o_free[ob], ((oc >> 1) - 1) & 1)))
+        return false;
+      lsum[(ob * 2 + sg) * kM + r] = l;
+      if (sg == 0) mfin[ob * kM + r] = m;
+      if (warp == 2 && lane == 0) erec[ob] = er;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&l_ready[ob]);
+      return true;
+    };
     for (int it = 0; ok; ++it) {
       const int slot = it & 1;
       if (!__all_sync(0xffffffffu, mbar_wait_bounded(&it_full[slot], (it >> 1) & 1))) {
@@ -545,7 +572,10 @@ __global__ void __launch_bounds__(kThreadsP, 1)
       const PfItem rec = items[slot];
       __syncwarp();
       if (lane == 0) mbar_arrive(&it_empty[slot]);
-      if (rec.b < 0) break;
+      if (rec.b < 0) {  // no more items: an end record for the epilogue warps
+        if (!hand_off(oc & 1, make_int4(-1, 0, 0, 0), 0.f, 0.f)) ok = false;
+        break;
+      }
       const int rows_tok = min(tq, rec.lq - rec.t0);
       const bool row_ok = r < m_used && t < rows_tok;
       const int64_t orow = static_cast<int64_t>(rec.q_start + rec.t0 + t) * p.hq + rec.h * g + jh;
@@ -634,24 +664,47 @@ __global__ void __launch_bounds__(kThreadsP, 1)
         if (lane == 0) mbar_arrive(p_full);
       }
       if (!ok) break;
-      // ---- epilogue: O of this item is complete once its last P V is -------
+      if (!hand_off(ob, make_int4(rec.q_start + rec.t0, rec.h, rows_tok, 0), l, m)) {
+        ok = false;
+        break;
+      }
+      ++oc;
+    }
+  } else {
+    // ======================= epilogue (warps 10..13) =========================
+    // Thread = TMEM lane = packed query row, all head_dim columns. Per item
+    // (in the order the softmax warps finish them, O buffers alternating):
+    // wait for the item's last P V (o_full) and its row sums (l_ready),
+    // normalise O, store it, release the O buffer (o_free).
+    const int qd = warp & 3;  // the TMEM lane quarter this warp may access
+    const int r = qd * 32 + lane;
+    const int t = r / g, jh = r % g;
+    const uint32_t lane_base = static_cast<uint32_t>(qd * 32) << 16;
+    const float *lsum = reinterpret_cast<const float *>(smem + L::LSUM_OFF);
+    const float *mfin = reinterpret_cast<const float *>(smem + L::MFIN_OFF);
+    const int4 *erec = reinterpret_cast<const int4 *>(smem + L::EREC_OFF);
+    for (int oc = 0; ok; ++oc) {
+      const int ob = oc & 1;
+      if (!__all_sync(0xffffffffu, mbar_wait_bounded(&l_ready[ob], (oc >> 1) & 1))) {
+        ok = false;
+        break;
+      }
+      const int4 er = erec[ob];  // token base, KV head, query tokens; x < 0: the end
+      if (er.x < 0) break;
+      const float l = lsum[(ob * 2) * kM + r] + lsum[(ob * 2 + 1) * kM + r];
+      const float m = mfin[ob * kM + r];
       if (!__all_sync(0xffffffffu, mbar_wait_bounded(&o_full[ob], (oc >> 1) & 1))) {
         ok = false;
         break;
       }
-      xsum[sg * kM + r] = l;
-      __syncwarp();
-      if (lane == 0) mbar_arrive(lxch);
-      if (!__all_sync(0xffffffffu, mbar_wait_bounded(lxch, oc & 1))) {
-        ok = false;
-        break;
-      }
-      l += xsum[(sg ^ 1) * kM + r];
       tc_fence_after();
+      const bool row_ok = r < m_used && t < er.z;
+      const int64_t orow = static_cast<int64_t>(er.x + t) * p.hq + er.y * g + jh;
       const float inv = l > 0.f ? 1.f / l : 0.f;
-      T *o = static_cast<T *>(p.out) + orow * D + sg * OC;
+      T *o = static_cast<T *>(p.out) + orow * D;
+      const uint32_t tmem_o = tmem + L::O_COL + ob * L::OB_STRIDE;
 #pragma unroll
-      for (int c = 0; c < OC / 32; ++c) {
+      for (int c = 0; c < D / 32; ++c) {
         float ov[32];
         tmem_ld32(tmem_o + lane_base + c * 32, ov);
         tmem_wait_ld();
@@ -667,12 +720,10 @@ __global__ void __launch_bounds__(kThreadsP, 1)
           }
         }
       }
-      if (row_ok && p.lse && sg == 0)
-        p.lse[orow] = l > 0.f ? (m + __log2f(l)) * kLn2 : -INFINITY;
+      if (row_ok && p.lse) p.lse[orow] = l > 0.f ? (m + __log2f(l)) * kLn2 : -INFINITY;
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&o_free[ob]);  // O buffer ob may be overwritten
-      ++oc;
     }
   }
   if (!ok && lane == 0) flag(p.status, MI_STATUS_TIMEOUT);
