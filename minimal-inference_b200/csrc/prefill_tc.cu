@@ -229,8 +229,15 @@ __global__ void __launch_bounds__(kThreadsP, 1)
   const int m_used = tq * g;    // packed rows in use
 
   // ---- once per CTA: query-tile prefix over requests, barriers, TMEM ------
+  // qo_indptr entries are clamped to [0, total_q] and a request whose range
+  // ends before it starts gets no rows, so no output row at or past total_q
+  // is ever written; such an indptr is flagged (query rows left out)
+  auto qo_at = [&](int i) { return min(max(p.qo_indptr[i], 0), p.total_q); };
   for (int i = threadIdx.x; i <= p.batch; i += blockDim.x) {
-    s_qo[i] = p.qo_indptr[i];
+    const int v = qo_at(i);
+    if (blockIdx.x == 0 && (v != p.qo_indptr[i] || (i < p.batch && qo_at(i + 1) < v)))
+      flag(p.status, MI_STATUS_BAD_POSITION);
+    s_qo[i] = v;
     s_ip[i] = p.indptr[i];
     if (i < p.batch) s_lk[i] = kv_len_of(p.indptr, p.last, i, p.ps);
   }
@@ -239,7 +246,7 @@ __global__ void __launch_bounds__(kThreadsP, 1)
     if (lane == 0) tiles_pre[0] = 0;
     for (int base = 0; base < p.batch; base += 32) {
       const int bb = base + lane;
-      int x = bb < p.batch ? cdiv(p.qo_indptr[bb + 1] - p.qo_indptr[bb], tq) : 0;
+      int x = bb < p.batch ? cdiv(max(0, qo_at(bb + 1) - qo_at(bb)), tq) : 0;
 #pragma unroll
       for (int o = 1; o < 32; o <<= 1) {
         const int y = __shfl_up_sync(0xffffffffu, x, o);

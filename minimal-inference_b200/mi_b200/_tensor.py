@@ -45,3 +45,27 @@ def check_pool(kv: torch.Tensor):
         raise ValueError("paged kv cache must be contiguous")
     p, _, ps, hkv, d = kv.shape
     return p, ps, hkv, d
+
+
+def need_on(name: str, t: torch.Tensor, device) -> torch.Tensor:
+    """``t`` must live on ``device``: a kernel given another device's (or host)
+    memory would read or write through a pointer it cannot use."""
+    if t.device != torch.device(device):
+        raise ValueError(f"{name} is on {t.device}, expected {device}")
+    return t
+
+
+def check_rows(name: str, t: torch.Tensor, min_rows: int, row_shape: tuple, dtype: torch.dtype,
+               device) -> torch.Tensor:
+    """A caller-provided output the kernels write as dense rows: ``[>= min_rows,
+    *row_shape]``, contiguous, of ``dtype`` on ``device``."""
+    if (t.dim() != 1 + len(row_shape) or t.shape[0] < min_rows
+            or tuple(t.shape[1:]) != tuple(row_shape)):
+        raise ValueError(f"{name} must be [>= {min_rows}, {', '.join(map(str, row_shape))}], "
+                         f"got {tuple(t.shape)}")
+    if t.dtype != dtype:
+        raise ValueError(f"{name} must be {dtype}, got {t.dtype}")
+    if not t.is_contiguous():
+        raise ValueError(f"{name} must be contiguous")
+    return need_on(name, t, device)
+

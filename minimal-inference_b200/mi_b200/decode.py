@@ -14,7 +14,7 @@ import math
 import torch
 
 from . import capi
-from ._tensor import check_pool, dtype_code, need_i32, ptr, stream_of
+from ._tensor import check_pool, check_rows, dtype_code, need_i32, need_on, ptr, stream_of
 
 
 class BatchDecodeWithPagedKVCacheWrapper:
@@ -71,11 +71,16 @@ class BatchDecodeWithPagedKVCacheWrapper:
             raise ValueError(f"q must be [{b}, {pl['hq']}, {d}], got {tuple(q.shape)}")
         if q.stride(-1) != 1 or q.dtype != paged_kv_cache.dtype:
             raise ValueError("q needs the pool dtype and a unit stride on head_dim")
+        dev = self._ws.device
+        need_on("q", q, dev)
+        need_on("paged_kv_cache", paged_kv_cache, dev)
         if out is None:
             out = torch.empty((b, pl["hq"], d), dtype=q.dtype, device=q.device)
-        elif out.shape[0] < b or not out.is_contiguous() or out.dtype != q.dtype:
-            raise ValueError("out must be a contiguous [B, Hq, D] tensor of q's dtype")
-        if (return_lse or lse is not None) and lse is None:
+        else:
+            check_rows("out", out, b, (pl["hq"], d), q.dtype, dev)
+        if lse is not None:
+            check_rows("lse", lse, b, (pl["hq"],), torch.float32, dev)
+        elif return_lse:
             lse = torch.empty((b, pl["hq"]), dtype=torch.float32, device=q.device)
         capi.call(
             "mi_paged_decode",

@@ -11,7 +11,7 @@ from __future__ import annotations
 import torch
 
 from . import capi
-from ._tensor import check_pool, dtype_code, need_i32, ptr, stream_of
+from ._tensor import check_pool, dtype_code, need_i32, need_on, ptr, stream_of
 
 
 def append_paged_kv_cache(append_key: torch.Tensor, append_value: torch.Tensor,
@@ -58,6 +58,8 @@ def append_paged_kv_cache(append_key: torch.Tensor, append_value: torch.Tensor,
             raise ValueError("rope tables must be [max_pos, head_dim] in the pool dtype")
         if not (rope_cos.is_contiguous() and rope_sin.is_contiguous()):
             raise ValueError("rope tables must be contiguous")
+        need_on("rope_cos", rope_cos, dev)
+        need_on("rope_sin", rope_sin, dev)
         rope_max = rope_cos.shape[0]
     if rope_positions is not None:
         need_i32("rope_positions", rope_positions, dev)
@@ -70,6 +72,8 @@ def append_paged_kv_cache(append_key: torch.Tensor, append_value: torch.Tensor,
             raise ValueError("q/q_out must be [nnz, Hq, D]")
         if q.stride(-1) != 1 or q_out.stride(-1) != 1 or q.dtype != dt or q_out.dtype != dt:
             raise ValueError("q/q_out need the pool dtype and a unit stride on head_dim")
+        need_on("q", q, dev)
+        need_on("q_out", q_out, dev)
     if status is not None:
         need_i32("status", status, dev)
     capi.call(

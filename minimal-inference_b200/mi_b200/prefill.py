@@ -12,7 +12,7 @@ import math
 import torch
 
 from . import capi
-from ._tensor import check_pool, dtype_code, need_i32, ptr, stream_of
+from ._tensor import check_pool, check_rows, dtype_code, need_i32, need_on, ptr, stream_of
 
 
 class BatchPrefillWithPagedKVCacheWrapper:
@@ -75,9 +75,16 @@ class BatchPrefillWithPagedKVCacheWrapper:
             raise ValueError(f"q must be [total_q, {pl['hq']}, {d}], got {tuple(q.shape)}")
         if q.stride(-1) != 1 or q.dtype != paged_kv_cache.dtype:
             raise ValueError("q needs the pool dtype and a unit stride on head_dim")
+        dev = self._ws.device
+        need_on("q", q, dev)
+        need_on("paged_kv_cache", paged_kv_cache, dev)
         if out is None:
             out = torch.empty((total_q, pl["hq"], d), dtype=q.dtype, device=q.device)
-        if (return_lse or lse is not None) and lse is None:
+        else:
+            check_rows("out", out, total_q, (pl["hq"], d), q.dtype, dev)
+        if lse is not None:
+            check_rows("lse", lse, total_q, (pl["hq"],), torch.float32, dev)
+        elif return_lse:
             lse = torch.empty((total_q, pl["hq"]), dtype=torch.float32, device=q.device)
         ws_bytes = self._ws.numel() * self._ws.element_size()
         capi.call(

@@ -17,7 +17,7 @@ import torch
 import torch.distributed as dist
 
 from . import capi
-from ._tensor import dtype_code, stream_of
+from ._tensor import check_rows, dtype_code, stream_of
 
 MAX_ROWS = 256          # the kernel's flag slots per rank
 _FLAG_BYTES_PER_RANK = MAX_ROWS * 4
@@ -80,10 +80,22 @@ class PeerAllReduce:
     def reduce_add_norm(self, i: int, rows: int, residual: torch.Tensor, weight: torch.Tensor,
                         eps: float, out: torch.Tensor | None = None) -> torch.Tensor:
         """residual += all-reduce(site i partial); return rms_norm(residual) * weight."""
+        if not self.usable(rows):
+            raise ValueError(f"rows {rows} outside (0, {self.max_rows}]")
+        if not 0 <= i < self.num_sites:
+            raise IndexError(f"call site {i} of {self.num_sites}")
         if residual.shape[-1] != self.hidden or residual.numel() != rows * self.hidden:
             raise ValueError("residual must hold rows x hidden elements")
+        check_rows("residual", residual.reshape(rows, self.hidden) if residual.is_contiguous()
+                   else residual, rows, (self.hidden,), self.dtype, self.device)
+        check_rows("weight", weight.unsqueeze(0), 1, (self.hidden,), self.dtype, self.device)
         if out is None:
             out = torch.empty_like(residual)
+        elif out.shape != residual.shape:
+            raise ValueError("out must have the residual's shape")
+        else:
+            check_rows("out", out.reshape(rows, self.hidden) if out.is_contiguous() else out,
+                       rows, (self.hidden,), self.dtype, self.device)
         capi.call("mi_allreduce_add_rmsnorm", self.peer_bases.data_ptr(),
                   self.data_off0 + i * self.site_bytes, self.flag_off,
                   self.counters.data_ptr(), self.rank, self.world, residual.data_ptr(),

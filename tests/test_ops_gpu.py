@@ -325,6 +325,32 @@ def test_prefill_repeated_calls_share_workspace(ws_bytes):
         np.testing.assert_allclose(f32(out), want, atol=TOL[dtype], rtol=0)
 
 
+def test_prefill_qo_indptr_past_q_is_flagged_and_stays_in_bounds():
+    """A qo_indptr that claims more query rows than q holds (request 1: 80
+    rows, q has 30 of them) is clamped on the device and flagged
+    BAD_POSITION: nothing is written past total_q (a guard region behind
+    ``out`` stays zero) and request 0, wholly inside q, is still exact."""
+    from mi_b200 import capi
+    from mi_b200.prefill import BatchPrefillWithPagedKVCacheWrapper
+    hq, hkv, d, dtype = 32, 8, 128, "bfloat16"
+    c = paged_case(55, [40, 80], hq, hkv, d, dtype=dtype)
+    total_q = 70
+    rng = np.random.default_rng(56)
+    q = po.round_to(rng.standard_normal((total_q, hq, d), dtype=np.float32), dtype)
+    w = BatchPrefillWithPagedKVCacheWrapper(torch.empty(1 << 20, dtype=torch.uint8, device=DEV))
+    w.plan(i32(np.array([0, 40, 120], np.int32)), i32(c["indptr"]), i32(c["indices"]),
+           i32(c["last"]), hq, hkv, d, c["ps"], causal=True, q_data_type=tdt(dtype))
+    out_full = torch.zeros(total_q + 64, hq, d, dtype=tdt(dtype), device=DEV)
+    w.run(to_dev(q, dtype), to_dev(c["pool"], dtype), out=out_full[:total_q])
+    torch.cuda.synchronize()
+    with pytest.raises(capi.MiError, match="BAD_POSITION"):
+        w.check_status()
+    assert not bool(out_full[total_q:].any())
+    want, _ = po.prefill_attention(q[:40], np.array([0, 40], np.int32), c["pool"],
+                                   c["indptr"][:2], c["indices"], c["last"][:1], 16, causal=True)
+    np.testing.assert_allclose(f32(out_full[:40]), want, atol=TOL[dtype], rtol=0)
+
+
 # --------------------------------------------------------------------------
 # the reference's own attention path, replayed through the GPU kernels
 # --------------------------------------------------------------------------
