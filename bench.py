@@ -707,7 +707,6 @@ def main():
     from datetime import timedelta
 
     from mi_b200.decode import BatchDecodeWithPagedKVCacheWrapper
-    from mi_b200.page import append_paged_kv_cache
     from mi_b200.rope import rope_tables
 
     rank, world, local = dist_env()
@@ -732,15 +731,12 @@ def main():
         last.append(n % ps or ps)
     i32 = lambda x: torch.tensor(x, dtype=torch.int32, device=dev)  # noqa: E731
     indptr_t, indices_t, last_t = i32(indptr), i32(indices), i32(last)
-    pos_t = i32([n - 1 for n in lens])
-    bidx_t = i32(list(range(b)))
     g = torch.Generator(device=dev).manual_seed(1234 + rank)
     pools = [torch.randn(P, 2, ps, hkv, d, device=dev, dtype=torch.bfloat16, generator=g)
              for _ in range(L)]
     q_raw = torch.randn(b, hq, d, device=dev, dtype=torch.bfloat16, generator=g)
     k_new = torch.randn(b, hkv, d, device=dev, dtype=torch.bfloat16, generator=g)
     v_new = torch.randn(b, hkv, d, device=dev, dtype=torch.bfloat16, generator=g)
-    q_rot = torch.empty_like(q_raw)
     out = torch.empty(b, hq, d, device=dev, dtype=torch.bfloat16)
     cos, sin = rope_tables(d, 32768, 1e6, torch.bfloat16, dev)
     ws = torch.zeros(128 * 1024 * 1024, dtype=torch.uint8, device=dev)
@@ -748,10 +744,9 @@ def main():
     dec.plan(indptr_t, indices_t, last_t, hq, hkv, d, ps, q_data_type=torch.bfloat16)
 
     def layer_step(pool, ev=None):
-        """One layer through the public API (validating wrappers)."""
-        append_paged_kv_cache(k_new, v_new, bidx_t, pos_t, pool, indices_t, indptr_t, last_t,
-                              rope_cos=cos, rope_sin=sin, q=q_raw, q_out=q_rot)
-        dec.run(q_rot, pool, out=out)
+        """One layer through the public API (validating wrappers): the decode
+        step with its append (RoPE, K/V into the pages) fused in."""
+        dec.run_with_append(q_raw, pool, k_new, v_new, cos, sin, out=out)
 
     # The timed loop calls the C ABI directly with arguments validated once by
     # the calls above, so host-side Python never limits the device time.
@@ -762,24 +757,20 @@ def main():
     status = dec.status
 
     def raw_args(pool):
-        app = (k_new.data_ptr(), k_new.stride(0), k_new.stride(1), v_new.data_ptr(),
-               v_new.stride(0), v_new.stride(1), bidx_t.data_ptr(), pos_t.data_ptr(), b,
-               pool.data_ptr(), P, ps, hkv, d, capi.DTYPE_BF16, indices_t.data_ptr(),
-               indptr_t.data_ptr(), b, cos.data_ptr(), sin.data_ptr(), cos.shape[0], None,
-               q_raw.data_ptr(), q_raw.stride(0), q_raw.stride(1), q_rot.data_ptr(),
-               q_rot.stride(0), q_rot.stride(1), hq, -1, status.data_ptr(), stream)
-        de = (q_rot.data_ptr(), q_rot.stride(0), q_rot.stride(1), pool.data_ptr(), P, ps, hkv,
-              d, capi.DTYPE_BF16, indptr_t.data_ptr(), indices_t.data_ptr(), last_t.data_ptr(),
-              b, hq, 1.0 / math.sqrt(d), out.data_ptr(), None, ws.data_ptr(), ws_bytes,
-              status.data_ptr(), stream)
-        return app, de
+        return (q_raw.data_ptr(), q_raw.stride(0), q_raw.stride(1),
+                k_new.data_ptr(), k_new.stride(0), k_new.stride(1),
+                v_new.data_ptr(), v_new.stride(0), v_new.stride(1),
+                cos.data_ptr(), sin.data_ptr(), cos.shape[0],
+                pool.data_ptr(), P, ps, hkv, d, capi.DTYPE_BF16,
+                indptr_t.data_ptr(), indices_t.data_ptr(), last_t.data_ptr(), b, hq,
+                1.0 / math.sqrt(d), out.data_ptr(), None, ws.data_ptr(), ws_bytes,
+                status.data_ptr(), stream)
 
     args_per_layer = [raw_args(pl) for pl in pools]
-    app_fn, dec_fn = lib.mi_append_paged_kv_cache, lib.mi_paged_decode
+    step_fn = lib.mi_paged_decode_append
 
     def raw_step(layer):
-        app, de = args_per_layer[layer]
-        return app_fn(*app) | dec_fn(*de)
+        return step_fn(*args_per_layer[layer])
 
     def barrier():
         if world > 1:
@@ -813,15 +804,16 @@ def main():
         for layer in range(L):
             rc |= raw_step(layer)
     t_end.record()
-    # Decode launch duration for the roofline: the same decode launches back
-    # to back over the layer pools (each pool is read once per pass, and the
-    # L pools together are far larger than L2), bracketed by one event pair.
+    # Launch duration for the roofline: the step's one launch pair (fused
+    # decode + split-K merge) back to back over the layer pools (each pool is
+    # read once per pass, and the L pools together are far larger than L2),
+    # bracketed by one event pair.
     kd = max(1, min(K, 20))
     d_start, d_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     d_start.record()
     for _ in range(kd):
         for layer in range(L):
-            rc |= dec_fn(*args_per_layer[layer][1])
+            rc |= raw_step(layer)
     d_end.record()
     if rc:
         raise capi.MiError(f"launch failed in the timed loop: {lib.mi_last_error().decode()}")
@@ -836,7 +828,7 @@ def main():
     ms_per_step = ms_total / K
     value = world * step_bytes * K / (ms_total / 1e3) / 1e9
     peak, peak_kind = read_peak()
-    achieved = decode_bytes(lens) / (dec_ms / 1e3) / 1e9
+    achieved = (decode_bytes(lens) + append_bytes(b)) / (dec_ms / 1e3) / 1e9
     traffic = read_traffic()
 
     # ---- end to end through the public API with host buffers -----------------
@@ -872,9 +864,7 @@ def main():
             for i in range(L):
                 cs.wait_event(ev_in[i])
                 qv, kv, vv = views[i]
-                append_paged_kv_cache(kv, vv, bidx_t, pos_t, pools[i], indices_t, indptr_t,
-                                      last_t, rope_cos=cos, rope_sin=sin, q=qv, q_out=q_rot)
-                dec.run(q_rot, pools[i], out=out_d[i])
+                dec.run_with_append(qv, pools[i], kv, vv, cos, sin, out=out_d[i])
                 ev_out[i].record(cs)
                 d2h.wait_event(ev_out[i])
                 with torch.cuda.stream(d2h):
@@ -919,9 +909,7 @@ def main():
             for i in range(L):
                 qv, kv, vv = views[i]
                 in_d[i].copy_(in_h[i], non_blocking=True)
-                append_paged_kv_cache(kv, vv, bidx_t, pos_t, pools[i], indices_t, indptr_t,
-                                      last_t, rope_cos=cos, rope_sin=sin, q=qv, q_out=q_rot)
-                dec.run(q_rot, pools[i], out=out_d[i])
+                dec.run_with_append(qv, pools[i], kv, vv, cos, sin, out=out_d[i])
                 o_h[i].copy_(out_d[i], non_blocking=True)
 
         eager_ms = timed(eager_step)
@@ -961,16 +949,17 @@ def main():
         "steps": K, "warmup": max(args.warmup, 3), "ms_per_step": round(ms_per_step, 4),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic", "config": workload_config(),
-        "roofline": {"bound": "hbm", "kernel": "decode_sk_kernel",
+        "roofline": {"bound": "hbm", "kernel": "decode_sk_kernel (append fused in)",
                      "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
-                     "traffic": traffic, "algorithmic_bytes": decode_bytes(lens),
+                     "traffic": traffic,
+                     "algorithmic_bytes": decode_bytes(lens) + append_bytes(b),
                      "avg_launch_us": round(dec_ms * 1e3, 2),
-                     "timing": (f"CUDA events around {kd * L} back-to-back decode launches "
-                                "(decode + split-K merge kernel each) over the layer pools"),
+                     "timing": (f"CUDA events around {kd * L} back-to-back launch pairs "
+                                "(fused append + decode, split-K merge) over the layer pools"),
                      "gpu_launches_roofline_loop": 2 * kd * L},
         "cpu_baseline": cpu, "e2e": e2e, "clocks": clk,
-        "gpu_launches": 3 * K * L,
+        "gpu_launches": 2 * K * L,
         "model_decode": model_line,
     }
     print(json.dumps(line), flush=True)

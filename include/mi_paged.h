@@ -130,6 +130,40 @@ int mi_paged_decode(
     mi_stream_t stream);
 
 /* ---------------------------------------------------------------------------
+ * Decode step with the append fused in (no single FlashInfer counterpart:
+ * it replaces the pair model.py:207-216 append_paged_kv_cache +
+ * model.py:235 run of a decode step).
+ *
+ * Each request b has one new token at position kv_len_b - 1 (kv_len from
+ * kv_indptr / kv_last_page_len, which already count it, as the reference's
+ * decode-step page table does, scheduler.py:862). k_new / v_new:
+ * [batch][num_kv_heads][head_dim], raw K (before RoPE) and V; q: raw
+ * queries. The call writes K rotated by RoPE at that position (the append's
+ * three roundings, model.py:92-107) and V into the token's page slot, and
+ * computes mi_paged_decode over the rotated q. Result and pages are bit for
+ * bit those of mi_append_paged_kv_cache(k_new, v_new, batch_indices =
+ * 0..batch-1, positions = kv_len - 1, rope tables, q_in = q, q_out)
+ * followed by mi_paged_decode(q_out), in one launch pair. rope_cos /
+ * rope_sin: [rope_max_pos][head_dim] in `dtype`; a position outside the
+ * table is flagged MI_STATUS_BAD_POSITION and left out. Rows and tables
+ * 16-byte aligned, strides multiples of 8 elements. Shapes outside the
+ * stream-K decode kernel (fp32, head_dim other than 64/128, group > 16,
+ * 1/2/4/8 KV heads only) return MI_ERR_UNSUPPORTED and launch nothing; the
+ * caller then makes the two calls.
+ * ------------------------------------------------------------------------- */
+int mi_paged_decode_append(
+    const void *q, int64_t q_stride_b, int64_t q_stride_h,
+    const void *k_new, int64_t k_stride_b, int64_t k_stride_h,
+    const void *v_new, int64_t v_stride_b, int64_t v_stride_h,
+    const void *rope_cos, const void *rope_sin, int32_t rope_max_pos,
+    void *kv_data, int64_t num_pages, int32_t page_size, int32_t num_kv_heads,
+    int32_t head_dim, int32_t dtype,
+    const int32_t *kv_indptr, const int32_t *kv_indices, const int32_t *kv_last_page_len,
+    int32_t batch_size, int32_t num_qo_heads, float sm_scale,
+    void *out, float *lse, void *workspace, size_t workspace_bytes, int32_t *status,
+    mi_stream_t stream);
+
+/* ---------------------------------------------------------------------------
  * Paged decode for callers that cannot allocate device memory.
  *
  * No counterpart in the reference. Some hosts manage all GPU memory through

@@ -82,15 +82,6 @@ __device__ __forceinline__ void copy_vec(T *dst, const T *src) {
   }
 }
 
-// One RoPE output element before its final rounding:
-// round(round(x*c) + round(r*s)) with the outer round done by the store.
-template <typename T>
-__device__ __forceinline__ float rope1(float x, float r, float c, float s) {
-  const float a = Elt<T>::to(Elt<T>::from(__fmul_rn(x, c)));
-  const float b = Elt<T>::to(Elt<T>::from(__fmul_rn(r, s)));
-  return __fadd_rn(a, b);
-}
-
 // Rotate chunk `c` of a head row: out = x*cos + rotate_half(x)*sin where
 // rotate_half(x) = cat(-x2, x1) (model.py:101-107).
 template <typename T, int VEC>

@@ -708,6 +708,65 @@ extern "C" int mi_paged_decode(
 }
 
 // ---------------------------------------------------------------------------
+// Decode step with the append fused in: request b's new token (position
+// kv_len_b - 1) is rotated and written into its page by the decode kernel
+// itself, and the raw queries are rotated as they are loaded. Same result as
+// mi_append_paged_kv_cache(k_new, v_new, batch_indices = 0..B-1, positions =
+// kv_len - 1, rope tables, q, q_out) followed by mi_paged_decode(q_out),
+// bit for bit, in one launch pair instead of three launches. Only the
+// stream-K kernel does it: other shapes return MI_ERR_UNSUPPORTED and launch
+// nothing, and the caller makes the two calls.
+// ---------------------------------------------------------------------------
+extern "C" int mi_paged_decode_append(
+    const void *q, int64_t q_stride_b, int64_t q_stride_h,
+    const void *k_new, int64_t k_stride_b, int64_t k_stride_h,
+    const void *v_new, int64_t v_stride_b, int64_t v_stride_h,
+    const void *rope_cos, const void *rope_sin, int32_t rope_max_pos,
+    void *kv_data, int64_t num_pages, int32_t page_size, int32_t num_kv_heads,
+    int32_t head_dim, int32_t dtype,
+    const int32_t *kv_indptr, const int32_t *kv_indices, const int32_t *kv_last_page_len,
+    int32_t batch_size, int32_t num_qo_heads, float sm_scale,
+    void *out, float *lse, void *workspace, size_t workspace_bytes, int32_t *status,
+    mi_stream_t stream) {
+  using namespace mi;
+  MI_REQUIRE(batch_size >= 0, "decode_append: negative batch_size");
+  if (batch_size == 0) return MI_OK;
+  MI_REQUIRE(q && k_new && v_new && rope_cos && rope_sin && kv_data && kv_indptr &&
+                 kv_indices && kv_last_page_len && out && workspace,
+             "decode_append: null pointer argument");
+  MI_REQUIRE(page_size > 0 && num_kv_heads > 0 && head_dim > 0 && num_pages > 0 &&
+                 rope_max_pos > 0,
+             "decode_append: bad pool geometry or RoPE table length");
+  MI_REQUIRE(num_qo_heads >= num_kv_heads && num_qo_heads % num_kv_heads == 0,
+             "decode_append: num_qo_heads %d is not a multiple of num_kv_heads %d",
+             num_qo_heads, num_kv_heads);
+  MI_REQUIRE(reinterpret_cast<uintptr_t>(workspace) % 256 == 0,
+             "decode_append: workspace must be 256-byte aligned");
+  const bool half_type = dtype == MI_DTYPE_BF16 || dtype == MI_DTYPE_F16;
+  if (!(half_type && (head_dim == 64 || head_dim == 128) &&
+        num_qo_heads / num_kv_heads <= 16 && batch_size <= kMaxBatch &&
+        reinterpret_cast<uintptr_t>(out) % 16 == 0))
+    return fail(MI_ERR_UNSUPPORTED, "decode_append: shape outside the fused kernel's coverage");
+  SkArgs sk{q, q_stride_b, q_stride_h, kv_data, num_pages, page_size, num_kv_heads,
+            head_dim, dtype, kv_indptr, kv_indices, kv_last_page_len, batch_size,
+            num_qo_heads, sm_scale, out, lse, workspace, workspace_bytes, status,
+            reinterpret_cast<cudaStream_t>(stream)};
+  sk.k_new = k_new;
+  sk.ksb = k_stride_b;
+  sk.ksh = k_stride_h;
+  sk.v_new = v_new;
+  sk.vsb = v_stride_b;
+  sk.vsh = v_stride_h;
+  sk.rope_cos = rope_cos;
+  sk.rope_sin = rope_sin;
+  sk.rope_max = rope_max_pos;
+  const int rc = launch_decode_sk(sk);
+  if (rc >= 0) return rc;
+  return fail(MI_ERR_UNSUPPORTED,
+              "decode_append: shape, alignment or workspace outside the fused kernel's coverage");
+}
+
+// ---------------------------------------------------------------------------
 // Paged decode for callers that cannot allocate device memory.
 //
 // Some hosts own every byte of GPU memory through their own allocator (a

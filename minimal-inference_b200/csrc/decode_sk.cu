@@ -74,13 +74,24 @@ struct SkParams {
   float *part_lse;   // [(grid + batch)][hq]
   int bar_off, rec_off, scr_off;
   int meta_off;  // >= 0: kv_indptr / kv_last_page_len staged in shared memory here
+  // Fused append (mi_paged_decode_append; k_new == nullptr: plain decode):
+  // request b's new token sits at position kv_len_b - 1. Its raw K is
+  // rotated like the append kernel's, K and V are written into their page
+  // slot and patched into the stage that holds that slot; q is raw and is
+  // rotated at the same position as it is loaded.
+  const void *k_new, *v_new;
+  int64_t ksb, ksh, vsb, vsh;
+  const void *rope_cos, *rope_sin;
+  int rope_max;
+  void *kv;  // the pool, for the new tokens' page writes
 };
 
 constexpr int kSmemBatch = 1024;  // requests whose metadata fits the shared-memory copy
 
 // A stage holds nt <= tps consecutive 16-token tiles of one run segment.
 // flags: 1 first stage of the segment, 2 last, 4 direct (request wholly in
-// this run); bits 8-15 per-tile bad-page mask; bits 16-19 nt; bits 20+ the
+// this run), 8 the segment reaches the request's last token; bits 8-15
+// per-tile bad-page mask; bits 16-19 nt; bits 20+ the
 // stage's ordinal within the segment.
 struct __align__(16) StageRec {
   int b, tok0, kvlen, flags;
@@ -222,7 +233,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           // everything but the issue itself is ready before the wait for a free slot
           const int s = k % S;
           const int flags = (j0 == 0 ? 1 : 0) | (j0 + nt >= ntiles ? 2 : 0) | (direct ? 4 : 0) |
-                            (badmask << 8) | (nt << 16) | ((ord & 2047) << 20);
+                            (end_b <= hi ? 8 : 0) | (badmask << 8) | (nt << 16) |
+                            ((ord & 2047) << 20);
           const uint32_t tx = static_cast<uint32_t>(nt - __popc(badmask)) * kTileBytes;
           const int dh = r % DH, which = r / DH;
           unsigned char *dst =
@@ -292,6 +304,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   float m0 = -INFINITY, l0 = 0.f, m1 = -INFINITY, l1 = 0.f;
   int segments = 0;
   bool timed_out = false;
+  // fused append: this lane's 16-byte chunk of the new token's K (rotated)
+  // or V row of head h, patched into the stage that holds the token
+  uint4 patch = make_uint4(0, 0, 0, 0);
+  bool have_patch = false;
+  constexpr int kChunks = D / 8;           // 16-byte chunks of a K or V row
+  const int pw_which = lane / kChunks;     // lane -> (K or V, chunk)
+  const int pw_cc = lane % kChunks;
 
   for (int k = 0;; ++k) {
     const int s = k % S;
@@ -324,6 +343,79 @@ __global__ void __launch_bounds__(kThreads, 1)
         qa[kk][2] = a2;
         qa[kk][3] = a3;
       }
+      have_patch = false;
+      if (p.k_new != nullptr) {
+        // fused append: the request's new token is its last, at kv_len - 1
+        const int pos = rec.kvlen - 1;
+        if (pos < 0 || pos >= p.rope_max) {
+          if (lane == 0) flag(p.status, MI_STATUS_BAD_POSITION);  // left out, q unrotated
+        } else {
+          const T *cr = static_cast<const T *>(p.rope_cos) + static_cast<int64_t>(pos) * D;
+          const T *sr = static_cast<const T *>(p.rope_sin) + static_cast<int64_t>(pos) * D;
+          // q: element d pairs with d + D/2, held by this lane in k-step kk + KS/2
+#pragma unroll
+          for (int kk = 0; kk < KS / 2; ++kk) {
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const int d = kk * 16 + 2 * tq + ((i & 2) ? 8 : 0);
+              const uint32_t cl = *reinterpret_cast<const uint32_t *>(cr + d);
+              const uint32_t sl = *reinterpret_cast<const uint32_t *>(sr + d);
+              const uint32_t ch = *reinterpret_cast<const uint32_t *>(cr + d + D / 2);
+              const uint32_t sh = *reinterpret_cast<const uint32_t *>(sr + d + D / 2);
+              const T *xl = reinterpret_cast<const T *>(&qa[kk][i]);
+              const T *xh = reinterpret_cast<const T *>(&qa[kk + KS / 2][i]);
+              const T *cle = reinterpret_cast<const T *>(&cl), *sle = reinterpret_cast<const T *>(&sl);
+              const T *che = reinterpret_cast<const T *>(&ch), *she = reinterpret_cast<const T *>(&sh);
+              uint32_t lo, hi;
+              T *loe = reinterpret_cast<T *>(&lo), *hie = reinterpret_cast<T *>(&hi);
+#pragma unroll
+              for (int e = 0; e < 2; ++e) {
+                const float x1 = Elt<T>::to(xl[e]), x2 = Elt<T>::to(xh[e]);
+                loe[e] = Elt<T>::from(rope1<T>(x1, -x2, Elt<T>::to(cle[e]), Elt<T>::to(sle[e])));
+                hie[e] = Elt<T>::from(rope1<T>(x2, x1, Elt<T>::to(che[e]), Elt<T>::to(she[e])));
+              }
+              qa[kk][i] = lo;
+              qa[kk + KS / 2][i] = hi;
+            }
+          }
+          // this segment holds the new token: lanes build their chunk (all
+          // lanes keep the flag, so the patch below runs warp-wide)
+          if (flags & 8) have_patch = true;
+          if ((flags & 8) && lane < 2 * kChunks) {
+            if (pw_which == 0) {
+              const T *kr = static_cast<const T *>(p.k_new) + static_cast<int64_t>(rec.b) * p.ksb +
+                            static_cast<int64_t>(h) * p.ksh;
+              const int half = kChunks / 2, pc = pw_cc < half ? pw_cc + half : pw_cc - half;
+              const uint4 xv = *reinterpret_cast<const uint4 *>(kr + pw_cc * 8);
+              const uint4 rv = *reinterpret_cast<const uint4 *>(kr + pc * 8);
+              const uint4 cv = *reinterpret_cast<const uint4 *>(cr + pw_cc * 8);
+              const uint4 sv = *reinterpret_cast<const uint4 *>(sr + pw_cc * 8);
+              const T *xe = reinterpret_cast<const T *>(&xv), *re = reinterpret_cast<const T *>(&rv);
+              const T *ce = reinterpret_cast<const T *>(&cv), *se = reinterpret_cast<const T *>(&sv);
+              T *pe = reinterpret_cast<T *>(&patch);
+#pragma unroll
+              for (int e = 0; e < 8; ++e) {
+                const float r = Elt<T>::to(re[e]);
+                pe[e] = Elt<T>::from(rope1<T>(Elt<T>::to(xe[e]), pw_cc < half ? -r : r,
+                                              Elt<T>::to(ce[e]), Elt<T>::to(se[e])));
+              }
+            } else {
+              const T *vr = static_cast<const T *>(p.v_new) + static_cast<int64_t>(rec.b) * p.vsb +
+                            static_cast<int64_t>(h) * p.vsh;
+              patch = *reinterpret_cast<const uint4 *>(vr + pw_cc * 8);
+            }
+            if (sw == 0) {  // one warp per head writes the token into its page slot
+              const int page = p.indices[ip[rec.b] + pos / p.ps];
+              if (page >= 0 && page < p.num_pages) {
+                T *dst = static_cast<T *>(p.kv) +
+                         ((static_cast<int64_t>(page) * 2 + pw_which) * p.ps + pos % p.ps) * (HKV * D) +
+                         h * D + pw_cc * 8;
+                *reinterpret_cast<uint4 *>(dst) = patch;
+              }
+            }
+          }
+        }
+      }
 #pragma unroll
       for (int n = 0; n < NT; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
       m0 = m1 = -INFINITY;
@@ -351,6 +443,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         __syncwarp();
         fence_proxy_async_smem();
+      }
+      if (have_patch) {
+        // fused append: the stage loaded the page before this step's token
+        // was written; put the new K / V row of head h in place
+        const int rn = rec.kvlen - 1 - (rec.tok0 + t * kTile);
+        if (rn >= 0 && rn < kTile) {
+          if (lane < 2 * kChunks && nvalid > rn) {
+            const int dh = pw_cc >> 3, c = pw_cc & 7;
+            *reinterpret_cast<uint4 *>(st + (pw_which * DH + dh) * block_bytes +
+                                       h * (kTile * 128) + swz(rn, c)) = patch;
+          }
+          __syncwarp();
+          have_patch = false;
+        }
       }
       float s0[4] = {0.f, 0.f, 0.f, 0.f}, s1[4] = {0.f, 0.f, 0.f, 0.f};
       {
@@ -731,6 +837,28 @@ int launch_decode_sk(const SkArgs &a) {
   p.rec_off = L.rec_off;
   p.scr_off = L.scr_off;
   p.meta_off = L.meta_off;
+  if (a.k_new != nullptr) {
+    // fused append: 16-byte rows of the new K / V and of the RoPE tables
+    const bool rows_ok =
+        a.v_new && a.rope_cos && a.rope_sin && a.rope_max > 0 &&
+        (reinterpret_cast<uintptr_t>(a.k_new) & 15) == 0 &&
+        (reinterpret_cast<uintptr_t>(a.v_new) & 15) == 0 &&
+        (reinterpret_cast<uintptr_t>(a.rope_cos) & 15) == 0 &&
+        (reinterpret_cast<uintptr_t>(a.rope_sin) & 15) == 0 && a.ksb % 8 == 0 &&
+        a.ksh % 8 == 0 && a.vsb % 8 == 0 && a.vsh % 8 == 0 &&
+        (reinterpret_cast<uintptr_t>(a.q) & 15) == 0 && a.qsb % 8 == 0 && a.qsh % 8 == 0;
+    if (!rows_ok) return -1;
+    p.k_new = a.k_new;
+    p.v_new = a.v_new;
+    p.ksb = a.ksb;
+    p.ksh = a.ksh;
+    p.vsb = a.vsb;
+    p.vsh = a.vsh;
+    p.rope_cos = a.rope_cos;
+    p.rope_sin = a.rope_sin;
+    p.rope_max = a.rope_max;
+    p.kv = const_cast<void *>(a.kv);
+  }
   const bool g16 = group > 8;
   if (a.dtype == MI_DTYPE_BF16) {
     if (a.d == 128)

@@ -21,6 +21,11 @@ struct SkArgs {
   size_t ws_bytes;
   int32_t *status;
   cudaStream_t stream;
+  // fused append (mi_paged_decode_append); k_new == nullptr: plain decode
+  const void *k_new = nullptr, *v_new = nullptr;
+  int64_t ksb = 0, ksh = 0, vsb = 0, vsh = 0;
+  const void *rope_cos = nullptr, *rope_sin = nullptr;
+  int rope_max = 0;
 };
 
 // Workspace bytes the stream-K kernel needs for this shape.

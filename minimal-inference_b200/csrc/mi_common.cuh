@@ -189,6 +189,17 @@ template <> struct Mma<__half> {
   }
 };
 
+// One RoPE output element before its final rounding (model.py:101-107):
+// round(round(x*c) + round(r*s)) with the outer round done by the store; no
+// FMA contraction, so pages and queries hold the reference's bits. Shared by
+// the append kernel and the decode kernel's fused append.
+template <typename T>
+__device__ __forceinline__ float rope1(float x, float r, float c, float s) {
+  const float a = Elt<T>::to(Elt<T>::from(__fmul_rn(x, c)));
+  const float b = Elt<T>::to(Elt<T>::from(__fmul_rn(r, s)));
+  return __fadd_rn(a, b);
+}
+
 // Programmatic dependent launch. A kernel launched with launch_pdl() may
 // start while its predecessor in the stream is still running; it must call
 // pdl_wait() before touching any memory (pdl_wait returns once every

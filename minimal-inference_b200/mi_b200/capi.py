@@ -16,6 +16,7 @@ LIB_PATH = os.path.join(_HERE, "libmi_paged.so")
 HEADER_PATH = os.path.join(os.path.dirname(os.path.dirname(_HERE)), "include", "mi_paged.h")
 
 DTYPE_F32, DTYPE_F16, DTYPE_BF16 = 0, 1, 2
+ERR_INVALID, ERR_UNSUPPORTED, ERR_WORKSPACE, ERR_CUDA = 1, 2, 3, 4
 STATUS_BITS = {
     1: "OUT_OF_PAGES", 2: "BAD_PAGE", 4: "BAD_POSITION", 8: "BAD_BATCH_INDEX",
     16: "POOL_OVERFLOW", 32: "SLOT_FULL", 64: "TIMEOUT",
@@ -45,6 +46,14 @@ _SIGS = {
     "mi_paged_decode_workspace_size": ([_c_i32, _c_i32, _c_i32, _c_i32], _c_size),
     "mi_paged_decode": ([
         _c_p, _c_i64, _c_i64,
+        _c_p, _c_i64, _c_i32, _c_i32, _c_i32, _c_i32,
+        _c_p, _c_p, _c_p, _c_i32, _c_i32, _c_f,
+        _c_p, _c_p, _c_p, _c_size, _c_p, _c_p], ctypes.c_int),
+    "mi_paged_decode_append": ([
+        _c_p, _c_i64, _c_i64,
+        _c_p, _c_i64, _c_i64,
+        _c_p, _c_i64, _c_i64,
+        _c_p, _c_p, _c_i32,
         _c_p, _c_i64, _c_i32, _c_i32, _c_i32, _c_i32,
         _c_p, _c_p, _c_p, _c_i32, _c_i32, _c_f,
         _c_p, _c_p, _c_p, _c_size, _c_p, _c_p], ctypes.c_int),

@@ -92,6 +92,80 @@ class BatchDecodeWithPagedKVCacheWrapper:
             self.status.data_ptr(), stream_of(q))
         return (out, lse) if return_lse else out
 
+    def run_with_append(self, q: torch.Tensor, paged_kv_cache: torch.Tensor,
+                        append_key: torch.Tensor, append_value: torch.Tensor,
+                        rope_cos: torch.Tensor, rope_sin: torch.Tensor,
+                        out: torch.Tensor | None = None,
+                        status: torch.Tensor | None = None,
+                        positions: torch.Tensor | None = None,
+                        scratch_page: int = -1) -> torch.Tensor:
+        """A decode step with its append fused in (extension, no FlashInfer
+        counterpart): ``q`` are the raw queries ``[B, Hq, D]``,
+        ``append_key``/``append_value`` the raw new K / V ``[B, Hkv, D]`` of
+        each request's token at position ``kv_len - 1`` (the planned page
+        table already counts it). Same pages and output, bit for bit, as
+        ``append_paged_kv_cache(k, v, arange(B), kv_len - 1, ..., rope tables,
+        q=q, q_out=q_rot)`` followed by ``run(q_rot)``; shapes the fused kernel
+        does not cover take exactly those two calls, with ``positions`` and
+        ``scratch_page`` passed to the append when given (a scheduler's
+        padded lanes have no pages and append into its scratch page; the
+        fused kernel leaves such lanes out). Device-side problems are
+        flagged in ``status`` (default: this wrapper's)."""
+        pl = self._plan
+        if pl is None:
+            raise RuntimeError("plan() must be called before run_with_append()")
+        num_pages, ps, hkv, d = check_pool(paged_kv_cache)
+        if (ps, hkv, d) != (pl["ps"], pl["hkv"], pl["d"]):
+            raise ValueError("paged kv cache geometry differs from plan()")
+        b, dt, dev = pl["batch"], paged_kv_cache.dtype, self._ws.device
+        need_on("paged_kv_cache", paged_kv_cache, dev)
+        for name, t, heads in (("q", q, pl["hq"]), ("append_key", append_key, hkv),
+                               ("append_value", append_value, hkv)):
+            if t.dim() != 3 or t.shape[0] < b or t.shape[1] != heads or t.shape[2] != d:
+                raise ValueError(f"{name} must be [{b}, {heads}, {d}], got {tuple(t.shape)}")
+            if t.stride(-1) != 1 or t.dtype != dt:
+                raise ValueError(f"{name} needs the pool dtype and a unit stride on head_dim")
+            need_on(name, t, dev)
+        for name, t in (("rope_cos", rope_cos), ("rope_sin", rope_sin)):
+            if t.dim() != 2 or t.shape[1] != d or t.dtype != dt or not t.is_contiguous():
+                raise ValueError(f"{name} must be a contiguous [max_pos, {d}] table of {dt}")
+            need_on(name, t, dev)
+        if rope_cos.shape != rope_sin.shape:
+            raise ValueError("rope_cos and rope_sin differ in shape")
+        if out is None:
+            out = torch.empty((b, pl["hq"], d), dtype=dt, device=dev)
+        else:
+            check_rows("out", out, b, (pl["hq"], d), dt, dev)
+        st = self.status if status is None else need_i32("status", status, dev)
+        lib = capi.lib()
+        rc = lib.mi_paged_decode_append(
+            q.data_ptr(), q.stride(0), q.stride(1),
+            append_key.data_ptr(), append_key.stride(0), append_key.stride(1),
+            append_value.data_ptr(), append_value.stride(0), append_value.stride(1),
+            rope_cos.data_ptr(), rope_sin.data_ptr(), rope_cos.shape[0],
+            paged_kv_cache.data_ptr(), num_pages, ps, hkv, d, dtype_code(dt),
+            pl["indptr"].data_ptr(), pl["indices"].data_ptr(), pl["last"].data_ptr(), b,
+            pl["hq"], pl["scale"], out.data_ptr(), None,
+            self._ws.data_ptr(), self._ws.numel() * self._ws.element_size(), st.data_ptr(),
+            stream_of(q))
+        if rc == capi.ERR_UNSUPPORTED:
+            from .page import append_paged_kv_cache
+            if positions is None:
+                npages = pl["indptr"][1:b + 1] - pl["indptr"][:b]
+                positions = ((npages - 1) * ps + pl["last"][:b] - 1).clamp(min=0)
+                positions = positions.to(torch.int32)
+            q_rot = torch.empty((b, pl["hq"], d), dtype=dt, device=dev)
+            append_paged_kv_cache(append_key[:b], append_value[:b],
+                                  torch.arange(b, dtype=torch.int32, device=dev), positions,
+                                  paged_kv_cache, pl["indices"], pl["indptr"], pl["last"],
+                                  rope_cos=rope_cos, rope_sin=rope_sin, q=q[:b], q_out=q_rot,
+                                  scratch_page=scratch_page, status=st)
+            return self.run(q_rot, paged_kv_cache, out=out)
+        if rc != 0:
+            msg = lib.mi_last_error().decode(errors="replace")
+            raise capi.MiError(f"mi_paged_decode_append failed (code {rc}): {msg}")
+        return out
+
     def check_status(self) -> None:
         """Synchronise and raise if a launch flagged a device-side problem."""
         w = int(self.status.item())

@@ -184,14 +184,23 @@ class Attention(nn.Module):
         be = attn_backend
         layer = be.next_layer()
         kv_data = be.paged_kv_cache.kv_data[layer]
-        q_rot = be.q_buffer(n, hq, d, x.dtype)
-        # RoPE on Q and K + K/V scatter into the pages: one launch
-        # (model.py:169-170, :203-216)
-        append_paged_kv_cache(k, v, be.batch_indices, be.positions, kv_data,
-                              be.kv_page_indices, be.kv_page_indptr, be.kv_last_page_len,
-                              rope_cos=be.rope_cos, rope_sin=be.rope_sin, q=q, q_out=q_rot,
-                              scratch_page=be.paged_kv_cache.scratch_page, status=be.status)
-        out = be.wrapper.run(q_rot, kv_data, out=be.out_buffer(n, hq, d, x.dtype))
+        if be.mode == "decode" and seq_len == 1:
+            # one new token per request: its append (RoPE on Q and K, K/V into
+            # the pages; model.py:169-170, :203-216) runs inside the decode
+            # kernel (model.py:235)
+            out = be.wrapper.run_with_append(
+                q, kv_data, k, v, be.rope_cos, be.rope_sin,
+                out=be.out_buffer(n, hq, d, x.dtype), status=be.status,
+                positions=be.positions, scratch_page=be.paged_kv_cache.scratch_page)
+        else:
+            q_rot = be.q_buffer(n, hq, d, x.dtype)
+            # RoPE on Q and K + K/V scatter into the pages: one launch
+            # (model.py:169-170, :203-216)
+            append_paged_kv_cache(k, v, be.batch_indices, be.positions, kv_data,
+                                  be.kv_page_indices, be.kv_page_indptr, be.kv_last_page_len,
+                                  rope_cos=be.rope_cos, rope_sin=be.rope_sin, q=q, q_out=q_rot,
+                                  scratch_page=be.paged_kv_cache.scratch_page, status=be.status)
+            out = be.wrapper.run(q_rot, kv_data, out=be.out_buffer(n, hq, d, x.dtype))
         if proj_out is not None:
             torch.mm(out.view(n, hq * d), self._o_wt, out=proj_out)
             return proj_out.view(bsz, seq_len, -1)

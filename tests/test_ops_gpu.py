@@ -256,6 +256,62 @@ def test_decode_workspace_reuse_and_page_size_8():
     check_decode(paged_case(31, [37, 64, 129, 1000], 32, 8, 128, page_size=32))
 
 
+def _append_then_decode_vs_fused(seed, lens, hq, hkv, d, ps, dtype):
+    """(pool, out) of append (RoPE) + decode and of the fused decode step on
+    the same inputs."""
+    from mi_b200.decode import BatchDecodeWithPagedKVCacheWrapper
+    from mi_b200.page import append_paged_kv_cache
+    from mi_b200.rope import rope_tables
+    c = paged_case(seed, lens, hq, hkv, d, page_size=ps, dtype=dtype)
+    rng = np.random.default_rng(seed + 1)
+    b = len(lens)
+    raw = lambda h: to_dev(po.round_to(rng.standard_normal((b, h, d), dtype=np.float32),  # noqa: E731
+                                       dtype), dtype)
+    q, k, v = raw(hq), raw(hkv), raw(hkv)
+    cos, sin = rope_tables(d, 8192, 1e6, tdt(dtype), DEV)
+    ip, ind, last = i32(c["indptr"]), i32(c["indices"]), i32(c["last"])
+    pools, outs = [], []
+    for fused in (False, True):
+        pool = to_dev(c["pool"], dtype)
+        w = BatchDecodeWithPagedKVCacheWrapper(torch.zeros(64 << 20, dtype=torch.uint8,
+                                                           device=DEV))
+        w.plan(ip, ind, last, hq, hkv, d, ps)
+        if fused:
+            out = w.run_with_append(q, pool, k, v, cos, sin)
+        else:
+            q_rot = torch.empty_like(q)
+            append_paged_kv_cache(k, v, i32(list(range(b))), i32([n - 1 for n in lens]), pool,
+                                  ind, ip, last, rope_cos=cos, rope_sin=sin, q=q, q_out=q_rot)
+            out = w.run(q_rot, pool)
+        torch.cuda.synchronize()
+        w.check_status()
+        pools.append(pool)
+        outs.append(out)
+    return pools, outs
+
+
+@pytest.mark.parametrize("hq,hkv,d,ps", [(32, 8, 128, 16), (28, 4, 128, 16), (16, 2, 128, 32),
+                                         (8, 1, 64, 16), (14, 2, 64, 16)])
+def test_decode_append_matches_append_then_decode(hq, hkv, d, ps):
+    """The fused decode step (the new token's RoPE'd K and V written into its
+    page by the decode kernel, q rotated as it is loaded) leaves the same
+    page bits and returns the same output bits as the append kernel followed
+    by decode: one-token requests, tokens at page starts and ends, long and
+    short contexts, requests cut across stream-K runs."""
+    lens = [1, 16, 17, 300, 1024, 33, 4000, 129, 2, 640]
+    (pa, pb), (oa, ob) = _append_then_decode_vs_fused(62, lens, hq, hkv, d, ps, "bfloat16")
+    assert torch.equal(pa.view(torch.int16), pb.view(torch.int16))
+    assert torch.equal(oa.view(torch.int16), ob.view(torch.int16))
+
+
+def test_decode_append_outside_the_fused_kernel_takes_the_two_calls():
+    """fp32 is outside the fused kernel: run_with_append makes the append and
+    decode calls itself, with the same result."""
+    (pa, pb), (oa, ob) = _append_then_decode_vs_fused(64, [5, 70, 300], 8, 2, 64, 16, "float32")
+    assert torch.equal(pa, pb)
+    assert torch.equal(oa, ob)
+
+
 def test_decode_bad_page_is_flagged():
     from mi_b200 import capi
     c = paged_case(40, [40, 40], 32, 8, 128)
