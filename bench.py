@@ -75,7 +75,7 @@ def read_peak():
     try:
         with open(p) as f:
             return float(json.load(f)["hbm_gbs"]), "measured"
-    except Exception:
+    except (OSError, KeyError, TypeError, ValueError):  # absent or malformed: the fallback
         return FALLBACK_HBM_GBS, "fallback"
 
 
