@@ -75,7 +75,7 @@ def read_peak():
     try:
         with open(p) as f:
             return float(json.load(f)["hbm_gbs"]), "measured"
-    except Exception:
+    except (OSError, KeyError, TypeError, ValueError):  # absent or malformed: the fallback
         return FALLBACK_HBM_GBS, "fallback"
 
 
@@ -622,6 +622,9 @@ def parse_args():
                     help="layer pools per step (32 = Mistral-7B; fewer only for profiling)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--shard", choices=["replicas", "heads"], default="replicas",
+                    help="config 2 on N GPUs: N replicas (weak scaling) or the KV heads "
+                         "split over the GPUs (strong scaling)")
     ap.add_argument("--no-model", action="store_true",
                     help="skip the Mistral-7B-shape decode measurement (config 3)")
     ap.add_argument("--workload",
@@ -672,15 +675,18 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
-def workload_config():
+def workload_config(shard="replicas", world=1):
     c = CFG
+    heads = shard == "heads" and world > 1
     return {"workload": "BASELINE config 2: Mistral-7B-shape paged KV append + decode "
                         "attention, 32 layers per step, B=32, ctx U[256,4096] seeded, "
                         "random non-contiguous page tables",
             "model": "Mistral-7B attention shape (32 Q / 8 KV heads, head_dim 128)",
             "global_batch": c["batch"], "seq_len": f"U[{c['ctx_lo']},{c['ctx_hi']}]",
             "layers_per_step": c["layers"], "page_size": c["page_size"],
-            "pages_per_layer_pool": c["num_pages"], "parallelism": "replicas",
+            "pages_per_layer_pool": c["num_pages"],
+            "parallelism": (f"heads{world}: each GPU holds {c['hkv'] // world} of the "
+                            f"{c['hkv']} KV heads of every page" if heads else "replicas"),
             "l2": "inputs larger than L2: each step streams 32 distinct layer pools "
                   "(~285 MB of KV per layer)"}
 
@@ -715,8 +721,15 @@ def main():
                                 device_id=torch.device("cuda", local))
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
-    c = CFG
-    c["layers"] = args.layers
+    CFG["layers"] = args.layers
+    c = dict(CFG)
+    heads = args.shard == "heads" and world > 1
+    if heads:
+        # head-sharded config 2: rank r decodes KV heads [r * hkv/N, (r+1) * hkv/N)
+        # (and their query heads) of every request; no exchange between ranks
+        if CFG["hkv"] % world:
+            raise SystemExit(f"--shard heads needs {CFG['hkv']} KV heads divisible by {world}")
+        c["hq"], c["hkv"] = CFG["hq"] // world, CFG["hkv"] // world
     b, hq, hkv, d, ps, P, L = (c["batch"], c["hq"], c["hkv"], c["head_dim"], c["page_size"],
                                c["num_pages"], c["layers"])
     lens = config2_lens(c["seed"], b, c["ctx_lo"], c["ctx_hi"])
@@ -824,11 +837,11 @@ def main():
     dec_ms = max_over_ranks(d_start.elapsed_time(d_end)) / (kd * L)
     dec.check_status()
 
-    step_bytes = L * (decode_bytes(lens) + append_bytes(b))
+    step_bytes = L * (decode_bytes(lens, c) + append_bytes(b, c))  # this rank's bytes
     ms_per_step = ms_total / K
     value = world * step_bytes * K / (ms_total / 1e3) / 1e9
     peak, peak_kind = read_peak()
-    achieved = (decode_bytes(lens) + append_bytes(b)) / (dec_ms / 1e3) / 1e9
+    achieved = (decode_bytes(lens, c) + append_bytes(b, c)) / (dec_ms / 1e3) / 1e9
     traffic = read_traffic()
 
     # ---- end to end through the public API with host buffers -----------------
@@ -947,13 +960,14 @@ def main():
     line = {
         "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
         "steps": K, "warmup": max(args.warmup, 3), "ms_per_step": round(ms_per_step, 4),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-        "data": "synthetic", "config": workload_config(),
+        "higher_is_better": True, "scaling": "strong" if heads else "weak",
+        "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic", "config": workload_config(args.shard, world),
         "roofline": {"bound": "hbm", "kernel": "decode_sk_kernel (append fused in)",
                      "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
-                     "traffic": traffic,
-                     "algorithmic_bytes": decode_bytes(lens) + append_bytes(b),
+                     "traffic": traffic if not heads else None,
+                     "algorithmic_bytes": decode_bytes(lens, c) + append_bytes(b, c),
                      "avg_launch_us": round(dec_ms * 1e3, 2),
                      "timing": (f"CUDA events around {kd * L} back-to-back launch pairs "
                                 "(fused append + decode, split-K merge) over the layer pools"),

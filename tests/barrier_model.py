@@ -1,0 +1,92 @@
+"""A small discrete-event model of a kernel's mbarrier protocol (test helper).
+
+Roles (warps, or one thread) are generators that yield the kernel's
+synchronisation steps in program order:
+
+* ``("wait", bar, n)``    wait for completion ``n`` of ``bar`` (the kernel
+                          waits on parity ``n & 1``);
+* ``("arrive", bar)``     one arrival;
+* ``("tma", bar)``        an asynchronous copy that completes on ``bar``
+                          at any later time, in any order;
+* ``("mma", tag)``        a tensor-core product, and
+* ``("commit", bar)``     an arrival on ``bar`` once every product issued
+                          before it has completed (products complete in
+                          issue order).
+
+``run`` interleaves the roles and the asynchronous completions at random.
+It raises ``AssertionError`` on a deadlock (nothing can move), on a wait
+that passes on another completion than the one it names (phase aliasing:
+a parity wait cannot tell completion ``n`` from ``n - 1`` or ``n + 2``) and
+on arrivals beyond a barrier's count.
+"""
+from __future__ import annotations
+
+import random
+
+
+class Bar:
+    def __init__(self, name: str, count: int):
+        self.name, self.count, self.arrived, self.done = name, count, 0, 0
+
+    def arrive(self) -> None:
+        self.arrived += 1
+        assert self.arrived <= self.count, f"{self.name}: arrivals beyond its count"
+        if self.arrived == self.count:
+            self.arrived = 0
+            self.done += 1
+
+
+def run(bars: dict, roles: dict, seed: int, max_steps: int = 10 ** 6) -> None:
+    rnd = random.Random(seed)
+    pending = []     # barriers with an asynchronous copy in flight
+    products = []    # in-order tensor-core queue: ("mma", tag) / ("commit", bar)
+    action = {name: None for name in roles}
+    alive = set(roles)
+    for _ in range(max_steps):
+        if not (alive or pending or products):
+            return
+        progress = False
+        order = sorted(alive)
+        rnd.shuffle(order)
+        for name in order:
+            act = action[name]
+            while True:
+                if act is None:
+                    try:
+                        act = next(roles[name])
+                    except StopIteration:
+                        alive.discard(name)
+                        progress = True
+                        break
+                kind = act[0]
+                if kind == "wait":
+                    bar, n = bars[act[1]], act[2]
+                    if (bar.done & 1) != (n & 1):
+                        assert bar.done == n + 1, (
+                            f"{name}: wait on {act[1]} for completion {n} passed at {bar.done}")
+                        act, progress = None, True
+                        continue
+                    assert bar.done <= n, (
+                        f"{name}: wait on {act[1]} for completion {n} aliased at {bar.done}")
+                    break
+                if kind == "arrive":
+                    bars[act[1]].arrive()
+                elif kind == "tma":
+                    pending.append(act[1])
+                else:
+                    products.append(act)
+                act, progress = None, True
+                if rnd.random() < 0.3:
+                    break
+            action[name] = act
+        if pending and rnd.random() < 0.5:
+            bars[pending.pop(rnd.randrange(len(pending)))].arrive()
+            progress = True
+        if products and rnd.random() < 0.5:
+            act = products.pop(0)
+            if act[0] == "commit":
+                bars[act[1]].arrive()
+            progress = True
+        if not progress and not pending and not products:
+            raise AssertionError(f"deadlock: {({n: action[n] for n in alive})}")
+    raise AssertionError("no end within the step limit")

@@ -62,3 +62,16 @@ def test_seeded_workloads_are_deterministic_and_in_range():
     assert [len(p) for p, _ in s1] == [len(p) for p, _ in s2]
     assert all(64 <= len(p) <= 2048 and 16 <= n <= 512 for p, n in s1)
     assert all(0 <= t < 1000 for p, _ in s1 for t in p)
+
+
+def test_head_sharded_config_names_its_split_and_bytes_add_up():
+    """--shard heads: each of N GPUs holds Hkv/N KV heads of every page, so
+    the per-rank algorithmic bytes of the KV stream are 1/N of the whole."""
+    assert bench.workload_config()["parallelism"] == "replicas"
+    assert bench.workload_config("heads", 4)["parallelism"].startswith("heads4: each GPU holds 2")
+    assert bench.workload_config("heads", 1)["parallelism"] == "replicas"
+    lens = bench.config2_lens()
+    full = bench.decode_bytes(lens)
+    quarter = bench.decode_bytes(lens, dict(bench.CFG, hq=8, hkv=2))
+    kv_full = sum(lens) * 8 * 128 * 2 * 2
+    assert full - quarter > 0.74 * kv_full   # the KV bytes shrink 4x; q/out and metadata stay small
