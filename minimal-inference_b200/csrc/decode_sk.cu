@@ -455,6 +455,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                                        h * (kTile * 128) + swz(rn, c)) = patch;
           }
           __syncwarp();
+          // the stage is refilled by TMA (async proxy) once released
+          fence_proxy_async_smem();
           have_patch = false;
         }
       }
