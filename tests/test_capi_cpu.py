@@ -61,3 +61,26 @@ def test_missing_library_fails_loudly(monkeypatch, tmp_path):
 
 def test_status_names():
     assert capi.status_names(1 | 64) == ["OUT_OF_PAGES", "TIMEOUT"]
+
+
+def _header_params() -> dict:
+    """Parameter count of every function declared in include/mi_paged.h."""
+    import re
+    with open(capi.HEADER_PATH) as f:
+        text = re.sub(r"/\*.*?\*/", "", f.read(), flags=re.S)
+    out = {}
+    for m in re.finditer(r"\b(mi_[a-z0-9_]+)\s*\(([^;{]*?)\)\s*;", text, flags=re.S):
+        params = m.group(2).strip()
+        out[m.group(1)] = 0 if params in ("", "void") else params.count(",") + 1
+    return out
+
+
+def test_ctypes_signatures_match_the_header():
+    """Every ctypes signature takes as many arguments as the header declares:
+    a call with a shifted argument list would hand a kernel wrong pointers."""
+    declared = _header_params()
+    assert declared, "no declarations parsed"
+    for name, n in declared.items():
+        assert name in capi._SIGS, f"{name} has no ctypes signature"
+        assert len(capi._SIGS[name][0]) == n, (
+            f"{name}: header declares {n} parameters, ctypes {len(capi._SIGS[name][0])}")
