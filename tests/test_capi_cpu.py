@@ -84,3 +84,26 @@ def test_ctypes_signatures_match_the_header():
         assert name in capi._SIGS, f"{name} has no ctypes signature"
         assert len(capi._SIGS[name][0]) == n, (
             f"{name}: header declares {n} parameters, ctypes {len(capi._SIGS[name][0])}")
+
+
+def test_ctypes_argument_types_match_the_header():
+    """Parameter by parameter: pointers bind as c_void_p, int32_t / int64_t /
+    size_t / float as their ctypes types (a swapped pair would pass a count
+    check)."""
+    import re
+    with open(capi.HEADER_PATH) as f:
+        text = re.sub(r"/\*.*?\*/", "", f.read(), flags=re.S)
+    scalar = {"int32_t": ctypes.c_int32, "int64_t": ctypes.c_int64, "size_t": ctypes.c_size_t,
+              "float": ctypes.c_float, "mi_stream_t": ctypes.c_void_p}
+    checked = 0
+    for m in re.finditer(r"\b(mi_[a-z0-9_]+)\s*\(([^;{]*?)\)\s*;", text, flags=re.S):
+        name, params = m.group(1), m.group(2).strip()
+        if params in ("", "void"):
+            continue
+        for i, p in enumerate(x.strip() for x in params.split(",")):
+            t = re.sub(r"\b[A-Za-z_][A-Za-z0-9_]*$", "", p).strip()
+            want = ctypes.c_void_p if "*" in t else scalar[t]
+            got = capi._SIGS[name][0][i]
+            assert got is want, f"{name} parameter {i} ({p}): ctypes {got.__name__}"
+            checked += 1
+    assert checked > 100
