@@ -139,24 +139,27 @@ class ClockSampler:
 # ---------------------------------------------------------------------------
 # CPU legs: the reference's own padded CPU path (ported in oracle/)
 # ---------------------------------------------------------------------------
-def cpu_reference_steps(lens, steps, budget_s=20.0):
+def cpu_reference_steps(lens, steps, budget_s=20.0, dtype_name="bfloat16"):
     """Time single-layer decode steps of the reference's CPU path.
 
     Returns (GB/s of algorithmic decode bytes, seconds, threads, sample text).
     The batch is cut to a prefix of the requests when the full batch would
-    not fit ``budget_s`` for ``steps`` steps.
+    not fit ``budget_s`` for ``steps`` steps. Bytes count the K/V, q and out
+    elements at the run's element size.
     """
     import torch
     from oracle.reference_cpu import PaddedDecodeLayer
     c = CFG
+    dt = getattr(torch, dtype_name)
+    elt = torch.empty((), dtype=dt).element_size()
     threads = torch.get_num_threads()
     b = len(lens)
-    layer = PaddedDecodeLayer(b, c["hkv"], c["ctx_hi"] + 1, c["head_dim"], torch.bfloat16)
+    layer = PaddedDecodeLayer(b, c["hkv"], c["ctx_hi"] + 1, c["head_dim"], dt)
     layer.fill([L - 1 for L in lens], seed=1)
     g = torch.Generator().manual_seed(2)
-    q = torch.randn(b, c["hq"], 1, c["head_dim"], generator=g).bfloat16()
-    kn = torch.randn(b, c["hkv"], 1, c["head_dim"], generator=g).bfloat16()
-    vn = torch.randn(b, c["hkv"], 1, c["head_dim"], generator=g).bfloat16()
+    q = torch.randn(b, c["hq"], 1, c["head_dim"], generator=g).to(dt)
+    kn = torch.randn(b, c["hkv"], 1, c["head_dim"], generator=g).to(dt)
+    vn = torch.randn(b, c["hkv"], 1, c["head_dim"], generator=g).to(dt)
     pos = [L - 1 for L in lens]
     t0 = time.perf_counter()
     layer.step(list(range(b)), pos, q, kn, vn)  # warm-up + per-step estimate
@@ -168,11 +171,14 @@ def cpu_reference_steps(lens, steps, budget_s=20.0):
     t0 = time.perf_counter()
     for _ in range(steps):
         layer.step(slots, pos[:nb], q[:nb], kn[:nb], vn[:nb])
-    dt = time.perf_counter() - t0
-    gbs = decode_bytes(lens[:nb]) * steps / dt / 1e9
+    secs = time.perf_counter() - t0
+    sub = lens[:nb]
+    elems = sum(sub) * c["hkv"] * c["head_dim"] * 2 + 2 * nb * c["hq"] * c["head_dim"]
+    nbytes = decode_bytes(sub) + (elt - 2) * elems  # decode_bytes counts 2-byte elements
+    gbs = nbytes * steps / secs / 1e9
     sample = (f"{steps} single-layer decode steps of the reference CPU path (padded cache + "
-              f"SDPA, bf16) over the first {nb} of the {b} config-2 requests")
-    return gbs, dt, threads, sample
+              f"SDPA, {dtype_name}) over the first {nb} of the {b} config-2 requests")
+    return gbs, secs, threads, sample
 
 
 # ---------------------------------------------------------------------------
@@ -945,6 +951,10 @@ def main():
         gbs, _, threads, sample = cpu_reference_steps(lens, 8, budget_s=20.0)
         cpu = {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
                "sample": sample}
+        # the same path in fp32 (the reference's CPU dtype for config 1)
+        gbs32, _, _, sample32 = cpu_reference_steps(lens, 4, budget_s=10.0,
+                                                    dtype_name="float32")
+        cpu["fp32"] = {"value": round(gbs32, 3), "unit": "GB/s", "sample": sample32}
 
     # ---- config 3: model decode tok/s (rank 0, N = 1) --------------------------
     model_line = None
