@@ -534,6 +534,83 @@ def prefill_flops(lens, hq=32, d=128) -> int:
     return sum(4 * hq * d * n * (n + 1) // 2 for n in lens)
 
 
+CONFIG1_PROMPT_LENS = (37, 128, 255, 500)
+
+
+def config1_prompts(vocab, seed=1):
+    rng = np.random.default_rng(seed)
+    return [rng.integers(0, vocab, n).tolist() for n in CONFIG1_PROMPT_LENS]
+
+
+def cpu_reference_config1(steps=8, seed=1234):
+    """The reference's CPU decode step at BASELINE config 1 (Qwen2.5-0.5B
+    shape, fp32, seeded weights, the 4 prompts of 37/128/255/500 tokens),
+    through the port of its whole padded forward (oracle/reference_cpu.py):
+    prefill of the 4 prompts, then ``steps`` batched decode steps. Returns
+    (mean ms per decode step, sample text)."""
+    import torch
+    from mi_b200.model import PRESETS, Model
+    from mi_b200.weights import init_random_weights
+    from oracle.reference_cpu import PaddedReferenceModel
+    cfg = PRESETS["qwen2.5-0.5b"]
+    model = Model(cfg)
+    init_random_weights(model, seed)
+    ref = PaddedReferenceModel(model.state_dict(), cfg, max_batch=4,
+                               max_seq=max(CONFIG1_PROMPT_LENS) + steps + 2)
+    del model
+    prompts = config1_prompts(cfg.vocab_size)
+    tokens = []
+    for slot, pr in enumerate(prompts):
+        tokens.append(int(ref.prefill(slot, pr).argmax()))
+    positions = [len(pr) for pr in prompts]
+    times = []
+    for _ in range(steps):
+        t0 = time.perf_counter()
+        logits = ref.decode(list(range(4)), positions, tokens)
+        times.append((time.perf_counter() - t0) * 1e3)
+        tokens = logits.argmax(-1).tolist()
+        positions = [p_ + 1 for p_ in positions]
+    ms = statistics.mean(times[1:]) if len(times) > 1 else times[0]
+    return ms, (f"{steps} batched decode steps (B=4, greedy) after the prefill of prompts "
+                f"{list(CONFIG1_PROMPT_LENS)}, fp32, {torch.get_num_threads()} threads; "
+                "mean of all but the first")
+
+
+def run_config1(args):
+    """BASELINE config 1 on one GPU: Qwen2.5-0.5B shape, fp32, the 4 prompts,
+    50 output tokens each, CUDA-graph decode; decode step time beside the
+    reference's CPU decode step on the same workload."""
+    import torch
+    from mi_b200.model import PRESETS, Model
+    from mi_b200.scheduler import Request, Scheduler
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    cfg = PRESETS["qwen2.5-0.5b"]
+    model = Model.create(cfg, dev, torch.float32, seed=1234)
+    prompts = config1_prompts(cfg.vocab_size)
+    sched = Scheduler(model, cfg, dev, torch.float32, max_batch_size=4, max_seq_len=1024,
+                      page_size=16, eos_token_ids=set())
+    for rep in range(2):   # warm-up set, then the measured one
+        reqs = [Request(f"c{rep}_{i}", p_, 50 if rep else 4, 0.0) for i, p_ in enumerate(prompts)]
+        for r in reqs:
+            sched.submit_request(r)
+        torch.cuda.synchronize()
+        step_ms = []
+        while sched.active_requests or sched.waiting_queue:
+            t0 = time.perf_counter()
+            sched.step()
+            step_ms.append((time.perf_counter() - t0) * 1e3)
+    gpu_ms = statistics.median(step_ms[1:])
+    del sched, model
+    torch.cuda.empty_cache()
+    cpu_ms, sample = cpu_reference_config1()
+    print(json.dumps({"metric": "config 1 decode step (Qwen2.5-0.5B shape, fp32, B=4)",
+                      "value": round(gpu_ms, 3), "unit": "ms", "higher_is_better": False,
+                      "n_gpus": 1, "cuda_graph_decode": True,
+                      "cpu_reference_ms": round(cpu_ms, 2), "cpu_sample": sample}),
+          flush=True)
+
+
 def run_prefill(args):
     """Kernel 3 on its own: ragged causal paged prefill of config 3's prompts.
 
@@ -634,7 +711,8 @@ def parse_args():
     ap.add_argument("--no-model", action="store_true",
                     help="skip the Mistral-7B-shape decode measurement (config 3)")
     ap.add_argument("--workload",
-                    choices=["config2", "config4", "config5", "prefill", "decode-shapes"],
+                    choices=["config2", "config1", "config4", "config5", "prefill",
+                             "decode-shapes"],
                     default="config2",
                     help="config5: Qwen2.5-72B tensor-parallel decode over the launch's GPUs; "
                          "prefill: the paged prefill kernel alone on config 3's prompts")
@@ -713,6 +791,9 @@ def main():
         return
     if args.workload == "decode-shapes":
         run_decode_shapes(args)
+        return
+    if args.workload == "config1":
+        run_config1(args)
         return
     import torch
     import torch.distributed as dist
@@ -955,6 +1036,10 @@ def main():
         gbs32, _, _, sample32 = cpu_reference_steps(lens, 4, budget_s=10.0,
                                                     dtype_name="float32")
         cpu["fp32"] = {"value": round(gbs32, 3), "unit": "GB/s", "sample": sample32}
+        # the reference's whole CPU decode step at config 1 (its own workload)
+        c1_ms, c1_sample = cpu_reference_config1()
+        cpu["config1_decode_step_ms"] = {"value": round(c1_ms, 2), "unit": "ms",
+                                         "sample": c1_sample}
 
     # ---- config 3: model decode tok/s (rank 0, N = 1) --------------------------
     model_line = None
