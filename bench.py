@@ -416,9 +416,10 @@ def run_tp_decode(args):
     t2t, dec_ms, first_s, init_s, capture_s = max_over_ranks(
         [t2t, dec_ms, first_s, init_s, capture_s])
     ok = all(len(r.generated_tokens) == steps + 1 for r in reqs)
+    sched.close()
     if model.comm is not None:
         model.comm.check_status()
-    sched.close()
+        model.comm.close()
     del sched, model
     if world > 1:
         dist.destroy_process_group()
@@ -872,6 +873,35 @@ def main():
     def raw_step(layer):
         return step_fn(*args_per_layer[layer])
 
+    # The same layer as two calls (the append kernel rotating q and writing
+    # K/V, then the plain decode), timed in the same window for comparison.
+    q_rot = torch.empty_like(q_raw)
+    bidx_t = torch.arange(b, dtype=torch.int32, device=dev)
+    pos_t = i32([n - 1 for n in lens])
+
+    def two_call_args(pool):
+        app = (k_new.data_ptr(), k_new.stride(0), k_new.stride(1),
+               v_new.data_ptr(), v_new.stride(0), v_new.stride(1),
+               bidx_t.data_ptr(), pos_t.data_ptr(), b,
+               pool.data_ptr(), P, ps, hkv, d, capi.DTYPE_BF16,
+               indices_t.data_ptr(), indptr_t.data_ptr(), b,
+               cos.data_ptr(), sin.data_ptr(), cos.shape[0], None,
+               q_raw.data_ptr(), q_raw.stride(0), q_raw.stride(1),
+               q_rot.data_ptr(), q_rot.stride(0), q_rot.stride(1), hq,
+               -1, status.data_ptr(), stream)
+        de = (q_rot.data_ptr(), q_rot.stride(0), q_rot.stride(1),
+              pool.data_ptr(), P, ps, hkv, d, capi.DTYPE_BF16,
+              indptr_t.data_ptr(), indices_t.data_ptr(), last_t.data_ptr(), b, hq,
+              1.0 / math.sqrt(d), out.data_ptr(), None, ws.data_ptr(), ws_bytes,
+              status.data_ptr(), stream)
+        return app, de
+
+    two_call_per_layer = [two_call_args(pl) for pl in pools]
+
+    def two_call_step(layer):
+        app, de = two_call_per_layer[layer]
+        return lib.mi_append_paged_kv_cache(*app) | lib.mi_paged_decode(*de)
+
     def barrier():
         if world > 1:
             dist.barrier(device_ids=[local])
@@ -915,6 +945,13 @@ def main():
         for layer in range(L):
             rc |= raw_step(layer)
     d_end.record()
+    # the two-call form of the same layers (append kernel, then plain decode)
+    c_start, c_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    c_start.record()
+    for _ in range(kd):
+        for layer in range(L):
+            rc |= two_call_step(layer)
+    c_end.record()
     if rc:
         raise capi.MiError(f"launch failed in the timed loop: {lib.mi_last_error().decode()}")
     torch.cuda.synchronize()
@@ -922,6 +959,7 @@ def main():
     clk = clocks.stop()
     ms_total = max_over_ranks(t_start.elapsed_time(t_end))
     dec_ms = max_over_ranks(d_start.elapsed_time(d_end)) / (kd * L)
+    two_call_ms = max_over_ranks(c_start.elapsed_time(c_end)) / (kd * L)
     dec.check_status()
 
     step_bytes = L * (decode_bytes(lens, c) + append_bytes(b, c))  # this rank's bytes
@@ -1064,8 +1102,11 @@ def main():
                      "traffic": traffic if not heads else None,
                      "algorithmic_bytes": decode_bytes(lens, c) + append_bytes(b, c),
                      "avg_launch_us": round(dec_ms * 1e3, 2),
+                     "two_call_us": round(two_call_ms * 1e3, 2),
                      "timing": (f"CUDA events around {kd * L} back-to-back launch pairs "
-                                "(fused append + decode, split-K merge) over the layer pools"),
+                                "(fused append + decode, split-K merge) over the layer pools; "
+                                "two_call_us: the same layers as the append kernel followed by "
+                                "the plain decode pair, timed right after"),
                      "gpu_launches_roofline_loop": 2 * kd * L},
         "cpu_baseline": cpu, "e2e": e2e, "clocks": clk,
         "gpu_launches": 2 * K * L,

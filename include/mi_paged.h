@@ -149,7 +149,11 @@ int mi_paged_decode(
  * 16-byte aligned, strides multiples of 8 elements. Shapes outside the
  * stream-K decode kernel (fp32, head_dim other than 64/128, group > 16,
  * 1/2/4/8 KV heads only) return MI_ERR_UNSUPPORTED and launch nothing; the
- * caller then makes the two calls.
+ * caller then makes the two calls. The launch may start before the kernel
+ * issued just before it on `stream` has finished (programmatic dependent
+ * launch) and reads kv_data from the start: that kernel must not write
+ * kv_data (a GEMM producing q / k_new / v_new is fine; an append into the
+ * same pool is not).
  * ------------------------------------------------------------------------- */
 int mi_paged_decode_append(
     const void *q, int64_t q_stride_b, int64_t q_stride_h,
@@ -177,13 +181,17 @@ int mi_paged_decode_append(
  * q, the pool, the page tables and out.
  *   - Limit: batch_size * num_kv_heads counters plus one partial slot per
  *     (request, KV head) of group*head_dim*4 bytes must fit in the array;
- *     larger calls return MI_ERR_WORKSPACE and launch nothing.
+ *     larger calls return MI_ERR_WORKSPACE and launch nothing. The limit
+ *     applies only to calls that the split-K kernels serve (16-bit dtypes,
+ *     head_dim 64/128, group <= 16, batch <= 2048, 16-byte aligned rows);
+ *     other calls run the generic kernel, which uses no scratch.
  *   - All calls share the array. Each call first clears its counters on
  *     `stream`; calls that overlap on the GPU (other streams, unordered
  *     threads) race on the array and must be serialised by the caller.
  *   - The first call on each device looks up the array's device address
- *     (once per device, with that device current); make that first call
- *     before any stream capture.
+ *     (with that device current) and caches it with the device's context;
+ *     after a device reset the next call looks it up again. Make the first
+ *     call on a device before any stream capture.
  * ------------------------------------------------------------------------- */
 #define MI_DECODE_STATIC_SCRATCH_BYTES (8u << 20)
 int mi_paged_decode_noalloc(
@@ -322,13 +330,32 @@ int mi_silu_mul(const void *gate_up, void *out, int32_t rows, int32_t inter, int
  * as the all-reduce result, then as the add), out[r] = rms_norm(residual[r])
  * * weight. rows <= 256. Every rank must make the same sequence of calls
  * (same rows); a call site's partial must not be rewritten before this
- * rank's next call has returned. Waits for peers are bounded (10 s): on
- * give-up MI_STATUS_TIMEOUT is set and the outputs are not written. */
+ * rank's next call has returned. Waits for peers are bounded (10 s by
+ * default, see mi_set_peer_wait_limit_ns): on give-up MI_STATUS_TIMEOUT is
+ * set and the outputs are not written. */
 int mi_allreduce_add_rmsnorm(const unsigned long long *peer_bases, int64_t data_off,
                              int64_t flag_off, uint32_t *block_counters, int32_t rank,
                              int32_t world, void *residual, const void *weight, void *out,
                              int32_t rows, int32_t hidden, float eps, int32_t dtype,
                              int32_t *status, mi_stream_t stream);
+
+/* Give-up limit (nanoseconds of GPU wall time) of the peer barrier in
+ * mi_allreduce_add_rmsnorm launches made after this call, process-wide;
+ * ns <= 0 restores the default of 10 s. No reference counterpart: a
+ * serving process lowers it to learn of a dead peer sooner. */
+int mi_set_peer_wait_limit_ns(int64_t ns);
+
+/* Peer mappings of the symmetric buffer (set-up calls, not for the hot
+ * path; no reference counterpart). Plain CUDA IPC: the peer's allocation is
+ * mapped over NVLink P2P and nothing is bound to an NVLink multicast object.
+ * mi_ipc_export: handle (MI_IPC_HANDLE_BYTES bytes) of the cudaMalloc
+ * allocation holding `ptr`, and ptr's byte offset in it. mi_ipc_open (in
+ * another process): map that allocation, *base_out = its base address here
+ * (add the offset). mi_ipc_close: unmap a base returned by mi_ipc_open. */
+#define MI_IPC_HANDLE_BYTES 64
+int mi_ipc_export(const void *ptr, void *handle_out, int64_t *offset_out);
+int mi_ipc_open(const void *handle, void **base_out);
+int mi_ipc_close(void *base);
 
 #ifdef __cplusplus
 }

@@ -20,13 +20,19 @@
 // this rank, which runs after this rank's kernel for the call in between has
 // passed its own barrier, i.e. after every peer finished reading it.
 // No multicast, no TMA: plain loads and stores over NVLink.
+#include <cuda.h>
+#include <string.h>
+
+#include <mutex>
+
 #include "mi_common.cuh"
 
 namespace mi {
 namespace {
 
 constexpr int kArBlocks = 256;  // max rows per call == flag slots per rank
-constexpr uint64_t kArWaitNs = 10000000000ull;  // 10 s: ranks may drift apart
+constexpr uint64_t kArWaitNs = 10000000000ull;  // 10 s default: ranks may drift apart
+std::atomic<uint64_t> g_peer_wait_ns{kArWaitNs};
 
 struct ArParams {
   const unsigned long long *peer_base;  // [world] each rank's buffer base, in this address space
@@ -39,6 +45,7 @@ struct ArParams {
   void *out;
   float eps;
   int32_t *status;
+  uint64_t wait_ns;  // give-up limit of the barrier with the peers
 };
 
 __device__ __forceinline__ void st_release_sys(unsigned *p, unsigned v) {
@@ -69,7 +76,7 @@ __global__ void __launch_bounds__(1024) ar_add_rmsnorm_kernel(const ArParams p) 
     for (int q = 0; q < p.world && ok; ++q) {
       if (q == p.rank) continue;
       for (uint32_t i = 0; static_cast<int>(ld_acquire_sys(mine + q * kArBlocks + b) - e) < 0; ++i) {
-        if ((i & 255u) == 255u && global_ns() - t0 > kArWaitNs) {
+        if ((i & 255u) == 255u && global_ns() - t0 > p.wait_ns) {
           ok = 0;
           break;
         }
@@ -178,7 +185,87 @@ extern "C" int mi_allreduce_add_rmsnorm(const unsigned long long *peer_bases, in
                  (reinterpret_cast<uintptr_t>(out) & 15) == 0,
              "allreduce: residual / weight / out must be 16-byte aligned");
   ArParams p{peer_bases, data_off, flag_off, block_counters, rank, world, rows, hidden,
-             residual, weight, out, eps, status};
+             residual, weight, out, eps, status, g_peer_wait_ns.load(std::memory_order_relaxed)};
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   return dtype == MI_DTYPE_BF16 ? launch_ar<__nv_bfloat16>(p, s) : launch_ar<__half>(p, s);
+}
+
+extern "C" int mi_set_peer_wait_limit_ns(int64_t ns) {
+  mi::g_peer_wait_ns.store(ns > 0 ? static_cast<uint64_t>(ns) : mi::kArWaitNs,
+                           std::memory_order_relaxed);
+  return MI_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Peer mappings for the symmetric buffer: plain CUDA IPC (cudaIpcGetMemHandle
+// / cudaIpcOpenMemHandle), which maps a peer's allocation over NVLink P2P and
+// binds nothing to an NVLink multicast object.
+// ---------------------------------------------------------------------------
+namespace mi {
+namespace {
+using AddrRangeFn = CUresult (*)(CUdeviceptr *, size_t *, CUdeviceptr);
+
+AddrRangeFn addr_range_fn() {
+  static AddrRangeFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void *ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuMemGetAddressRange", &ptr, 12000, cudaEnableDefault,
+                                         &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<AddrRangeFn>(ptr);
+  });
+  return fn;
+}
+}  // namespace
+}  // namespace mi
+
+extern "C" int mi_ipc_export(const void *ptr, void *handle_out, int64_t *offset_out) {
+  using namespace mi;
+  MI_REQUIRE(ptr && handle_out && offset_out, "ipc_export: null pointer argument");
+  static_assert(sizeof(cudaIpcMemHandle_t) <= MI_IPC_HANDLE_BYTES, "IPC handle size");
+  auto fn = addr_range_fn();
+  if (!fn) return fail(MI_ERR_CUDA, "ipc_export: cuMemGetAddressRange unavailable");
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  if (fn(&base, &size, reinterpret_cast<CUdeviceptr>(ptr)) != CUDA_SUCCESS)
+    return fail(MI_ERR_INVALID, "ipc_export: %p is not device memory", ptr);
+  cudaIpcMemHandle_t h;
+  const cudaError_t e = cudaIpcGetMemHandle(&h, reinterpret_cast<void *>(base));
+  if (e != cudaSuccess)
+    return fail(MI_ERR_CUDA,
+                "ipc_export: cudaIpcGetMemHandle: %s (memory from cudaMalloc is needed; "
+                "expandable segments of the caching allocator cannot be exported)",
+                cudaGetErrorString(e));
+  memset(handle_out, 0, MI_IPC_HANDLE_BYTES);
+  memcpy(handle_out, &h, sizeof(h));
+  *offset_out = static_cast<int64_t>(reinterpret_cast<CUdeviceptr>(ptr) - base);
+  return MI_OK;
+}
+
+extern "C" int mi_ipc_open(const void *handle, void **base_out) {
+  using namespace mi;
+  MI_REQUIRE(handle && base_out, "ipc_open: null pointer argument");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  void *base = nullptr;
+  const cudaError_t e = cudaIpcOpenMemHandle(&base, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return fail(MI_ERR_CUDA, "ipc_open: cudaIpcOpenMemHandle: %s", cudaGetErrorString(e));
+  }
+  *base_out = base;
+  return MI_OK;
+}
+
+extern "C" int mi_ipc_close(void *base) {
+  using namespace mi;
+  MI_REQUIRE(base, "ipc_close: null pointer");
+  const cudaError_t e = cudaIpcCloseMemHandle(base);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return fail(MI_ERR_CUDA, "ipc_close: cudaIpcCloseMemHandle: %s", cudaGetErrorString(e));
+  }
+  return MI_OK;
 }

@@ -28,6 +28,8 @@
 // (request, query head), warps split the tokens, online softmax per warp,
 // merged through shared memory. Used for fp32 parity configs and shapes the
 // fast path does not cover.
+#include <cuda.h>
+
 #include <mutex>
 
 #include "decode_sk.cuh"
@@ -618,6 +620,20 @@ int launch_tc(DecodeParams p, void *ws, size_t ws_bytes, cudaStream_t s) {
   return check_launch("decode_tc_kernel");
 }
 
+// Shapes and alignments the workspace kernels (stream-K, then the ticket
+// kernel) serve; every other call runs the generic kernel, which needs no
+// workspace.
+bool decode_fast_shape(const void *q, int64_t qsb, int64_t qsh, const void *kv, const void *out,
+                       int head_dim, int dtype, int group, int batch) {
+  const bool half_type = dtype == MI_DTYPE_BF16 || dtype == MI_DTYPE_F16;
+  const bool aligned = (reinterpret_cast<uintptr_t>(q) % 16 == 0) &&
+                       (reinterpret_cast<uintptr_t>(kv) % 16 == 0) &&
+                       (reinterpret_cast<uintptr_t>(out) % 16 == 0) && qsb % 8 == 0 &&
+                       qsh % 8 == 0;
+  return half_type && (head_dim == 64 || head_dim == 128) && group <= 16 && batch <= kMaxBatch &&
+         aligned;
+}
+
 template <typename T>
 int launch_fast(const DecodeParams &p, void *ws, size_t ws_bytes, cudaStream_t s) {
   const bool g16 = p.group > 8;
@@ -681,13 +697,9 @@ extern "C" int mi_paged_decode(
   p.lse = lse;
   p.status = status;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  const bool half_type = dtype == MI_DTYPE_BF16 || dtype == MI_DTYPE_F16;
-  const bool aligned = (reinterpret_cast<uintptr_t>(q) % 16 == 0) &&
-                       (reinterpret_cast<uintptr_t>(kv_data) % 16 == 0) &&
-                       (reinterpret_cast<uintptr_t>(out) % 16 == 0) && q_stride_b % 8 == 0 &&
-                       q_stride_h % 8 == 0;
-  const bool fast = half_type && (head_dim == 64 || head_dim == 128) && p.group <= 16 &&
-                    batch_size <= kMaxBatch && aligned && workspace != nullptr;
+  const bool fast = workspace != nullptr &&
+                    decode_fast_shape(q, q_stride_b, q_stride_h, kv_data, out, head_dim, dtype,
+                                      num_qo_heads / num_kv_heads, batch_size);
   if (fast) {
     MI_REQUIRE(reinterpret_cast<uintptr_t>(workspace) % 256 == 0,
                "decode: workspace must be 256-byte aligned");
@@ -785,11 +797,33 @@ namespace {
 
 constexpr int kMaxScratchDevices = 64;
 std::mutex g_scratch_mu;
-void *g_scratch_addr[kMaxScratchDevices] = {};
+struct ScratchSlot {
+  CUcontext ctx;  // the context the address belongs to
+  void *addr;
+};
+ScratchSlot g_scratch[kMaxScratchDevices] = {};
 
-// Device address of g_decode_scratch on the current device. Looked up once
-// per device (with that device current) and cached; in host code the array's
-// name is only a stand-in, never a usable pointer.
+using CtxGetCurrentFn = CUresult (*)(CUcontext *);
+
+CtxGetCurrentFn ctx_get_current_fn() {
+  static CtxGetCurrentFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void *ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuCtxGetCurrent", &ptr, 12000, cudaEnableDefault,
+                                         &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<CtxGetCurrentFn>(ptr);
+  });
+  return fn;
+}
+
+// Device address of g_decode_scratch on the current device. Looked up with
+// that device current and cached together with its context, so a device
+// reset (a new context, the array registered anew) makes the next call look
+// it up again; in host code the array's name is only a stand-in, never a
+// usable pointer.
 int scratch_address(void **out) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
@@ -798,16 +832,26 @@ int scratch_address(void **out) {
   if (dev < 0 || dev >= kMaxScratchDevices)
     return fail(MI_ERR_UNSUPPORTED, "decode_noalloc: device %d beyond %d", dev,
                 kMaxScratchDevices);
+  // the runtime makes the device's primary context current on first use
+  e = cudaFree(nullptr);
+  if (e != cudaSuccess)
+    return fail(MI_ERR_CUDA, "decode_noalloc: context set-up: %s", cudaGetErrorString(e));
+  CUcontext ctx = nullptr;
+  auto get_ctx = ctx_get_current_fn();
+  if (get_ctx == nullptr || get_ctx(&ctx) != CUDA_SUCCESS)
+    return fail(MI_ERR_CUDA, "decode_noalloc: cuCtxGetCurrent unavailable");
   std::lock_guard<std::mutex> lock(g_scratch_mu);
-  if (g_scratch_addr[dev] == nullptr) {
+  ScratchSlot &slot = g_scratch[dev];
+  if (slot.addr == nullptr || slot.ctx != ctx) {
     void *p = nullptr;
     e = cudaGetSymbolAddress(&p, g_decode_scratch);
     if (e != cudaSuccess || p == nullptr)
       return fail(MI_ERR_CUDA, "decode_noalloc: cudaGetSymbolAddress: %s",
                   cudaGetErrorString(e));
-    g_scratch_addr[dev] = p;
+    slot.ctx = ctx;
+    slot.addr = p;
   }
-  *out = g_scratch_addr[dev];
+  *out = slot.addr;
   return MI_OK;
 }
 
@@ -827,6 +871,14 @@ extern "C" int mi_paged_decode_noalloc(
   MI_REQUIRE(num_kv_heads > 0 && head_dim > 0 && num_qo_heads >= num_kv_heads &&
                  num_qo_heads % num_kv_heads == 0,
              "decode_noalloc: bad head counts %d / %d", num_qo_heads, num_kv_heads);
+  // Calls outside the workspace kernels' shapes run the generic kernel,
+  // which uses no scratch: no limit applies to them.
+  if (!decode_fast_shape(q, q_stride_b, q_stride_h, kv_data, out, head_dim, dtype,
+                         num_qo_heads / num_kv_heads, batch_size))
+    return mi_paged_decode(q, q_stride_b, q_stride_h, kv_data, num_pages, page_size,
+                           num_kv_heads, head_dim, dtype, kv_indptr, kv_indices,
+                           kv_last_page_len, batch_size, num_qo_heads, sm_scale, out, lse,
+                           nullptr, 0, status, stream);
   // Room for the counters plus at least one partial slot per (request, KV
   // head); anything larger than the fixed array is refused here.
   const size_t group = static_cast<size_t>(num_qo_heads / num_kv_heads);

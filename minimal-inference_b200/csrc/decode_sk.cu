@@ -57,6 +57,14 @@ constexpr int kTile = 16;
 constexpr int kMaxStages = 8;
 constexpr int kSmemLimit = 232448;        // 227 KB opt-in per CTA
 constexpr size_t kCtrl = 256;
+// Stream-K split: what a request start inside a run costs its CTA, in bytes
+// of page stream. A segment boundary stalls the CTA's consumers for ~3.5 us
+// (the previous segment's combine, the next one's query loads), about 154 KB
+// of one SM's share of HBM bandwidth; but a run shortened by k pages does
+// not finish k pages' time sooner, and on config 2 (B200, 8 KV heads) a
+// sweep of 154 / 300 / 450 / 650 KB gave 52.6 / 51.3 / 51.3 / 51.7 us per
+// launch pair.
+constexpr double kSegCostBytes = 380e3;
 
 inline size_t al256(size_t x) { return (x + 255) & ~size_t(255); }
 
@@ -74,6 +82,8 @@ struct SkParams {
   float *part_lse;   // [(grid + batch)][hq]
   int bar_off, rec_off, scr_off;
   int meta_off;  // >= 0: kv_indptr / kv_last_page_len staged in shared memory here
+  int rope_off;  // per consumer warp: the RoPE cos and sin rows of its segment's position
+  int seg_cost4;  // stream-K split: cost of a request start, in quarter pages (vsplit_run)
   // Fused append (mi_paged_decode_append; k_new == nullptr: plain decode):
   // request b's new token sits at position kv_len_b - 1. Its raw K is
   // rotated like the append kernel's, K and V are written into their page
@@ -96,6 +106,67 @@ constexpr int kSmemBatch = 1024;  // requests whose metadata fits the shared-mem
 struct __align__(16) StageRec {
   int b, tok0, kvlen, flags;
 };
+
+// Cost-balanced stream-K split, in virtual units of a quarter page. Page j
+// of a request b with n_b > 0 pages starts at virtual position
+//     vs_b + c4 + 4 j,   vs_b = 4 (indptr[b] - indptr[0]) + c4 * (non-empty
+//                                requests before b),
+// so every request's start is charged c4 quarter pages: the time a CTA's
+// consumers spend at a segment boundary (the previous segment's combine and
+// the next one's query loads), during which that CTA streams nothing. CTA i
+// owns the pages whose virtual start lies in [i R, (i+1) R), R =
+// max(4, ceil(VT / G)), VT = 4 * total + c4 * (non-empty requests): with c4 = 0 the
+// runs hold equal page counts, with c4 > 0 a CTA whose run holds more
+// request starts gets fewer pages. Warp-cooperative (all 32 lanes); `ip`
+// may be global or shared memory.
+__device__ __forceinline__ int vsplit_total(const int32_t *ip, int B, int c4, int lane) {
+  int nz = 0;
+  for (int b0 = 0; b0 < B; b0 += 32) {
+    const int b = b0 + lane;
+    nz += __popc(__ballot_sync(0xffffffffu, b < B && ip[b + 1] > ip[b]));
+  }
+  return 4 * (ip[B] - ip[0]) + c4 * nz;
+}
+
+// Page position (counted from indptr[0]) of the first page whose virtual
+// start is >= x.
+__device__ __forceinline__ int vsplit_page(const int32_t *ip, int B, int c4, int x, int lane) {
+  const int base0 = ip[0];
+  int nzpre = 0, best_b = -1, best_s = 0;
+  for (int b0 = 0; b0 < B; b0 += 32) {
+    const int b = b0 + lane;
+    const int np = b < B ? ip[b + 1] - ip[b] : 0;
+    const unsigned nzm = __ballot_sync(0xffffffffu, np > 0);
+    const int vs = 4 * ((b < B ? ip[b] : ip[B]) - base0) +
+                   c4 * (nzpre + __popc(nzm & ((1u << lane) - 1u)));
+    const unsigned cand = __ballot_sync(0xffffffffu, np > 0 && vs <= x);
+    if (cand) {
+      const int l = 31 - __clz(cand);
+      best_b = b0 + l;
+      best_s = __shfl_sync(0xffffffffu, vs, l);
+    }
+    nzpre += __popc(nzm);
+    if (__ballot_sync(0xffffffffu, b < B && vs > x)) break;  // later requests start past x
+  }
+  if (best_b < 0) return 0;
+  const int local = x - best_s - c4;
+  const int j = local <= 0 ? 0 : min(ip[best_b + 1] - ip[best_b], (local + 3) >> 2);
+  return ip[best_b] - base0 + j;
+}
+
+// Run length R. At least one page (4 units), so every run between the first
+// and the last run of a request holds a page of it and writes its partial.
+__device__ __forceinline__ int vsplit_len(int vt, int G) { return max(4, cdiv(vt, G)); }
+
+// This CTA's page range [lo, hi) (page positions from indptr[0]).
+__device__ __forceinline__ void vsplit_run(const int32_t *ip, int B, int c4, int G, int cta,
+                                           int lane, int *lo, int *hi) {
+  const int vt = vsplit_total(ip, B, c4, lane);
+  const int rv = vsplit_len(vt, G);
+  const int x0 = min(vt, cta * rv), x1 = min(vt, x0 + rv);
+  *lo = vsplit_page(ip, B, c4, x0, lane);
+  *hi = vsplit_page(ip, B, c4, x1, lane);
+}
 
 template <typename T, int D, bool G16, int HKV>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -136,8 +207,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   // append that writes this step's K/V and q) still runs. Everything up to
   // the pdl_wait() calls below reads only the page-table metadata
   // (kv_indptr / kv_indices / kv_last_page_len), which no kernel of this
-  // library that triggers its dependents early writes; the K/V tiles, q,
-  // the outputs and the workspace are touched only after pdl_wait().
+  // library that triggers its dependents early writes, and in the fused
+  // form the pool's pages; q, the outputs and the workspace are touched only
+  // after pdl_wait().
   // The producer's first page-id window only needs this CTA's run start, so
   // its loads go out together with the metadata staging below.
   int pre_pw = -1, pre_pwn = -1;
@@ -145,7 +217,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0)
       asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap)) : "memory");
     const int b0 = p.indptr[0], tot = p.indptr[p.batch] - b0;
-    const int lo0 = blockIdx.x * (tot > 0 ? cdiv(tot, gridDim.x) : 1);
+    int lo0, hi0;
+    vsplit_run(p.indptr, p.batch, p.seg_cost4, gridDim.x, blockIdx.x, lane, &lo0, &hi0);
     pre_pw = (lo0 + lane < tot) ? p.indices[b0 + lo0 + lane] : -1;
     pre_pwn = (lo0 + 32 + lane < tot) ? p.indices[b0 + lo0 + 32 + lane] : -1;
   }
@@ -165,16 +238,43 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   const int base0 = ip[0];
   const int total = ip[p.batch] - base0;
-  const int run = total > 0 ? cdiv(total, G) : 1;  // pages per CTA
+  int lo = 0, hi = 0;  // this CTA's pages (warp-cooperative split, every warp)
+  vsplit_run(ip, p.batch, p.seg_cost4, G, cta, lane, &lo, &hi);
 
   constexpr int block_bytes = kBlockBytes;
+
+  // L1 prefetch of the global rows a segment start of request b reads (see
+  // seg_begin below), spread over the producer's lanes: 128-byte lines.
+  auto prefetch_segment = [&](int b, int kvlen) {
+    constexpr int kLineRow = D * static_cast<int>(sizeof(T)) / 128;  // lines per head row
+    const char *qb = static_cast<const char *>(p.q) + static_cast<int64_t>(b) * p.qsb * sizeof(T);
+    for (int li = lane; li < p.hq * kLineRow; li += 32)
+      prefetch_l1(qb + (static_cast<int64_t>(li / kLineRow) * p.qsh * sizeof(T)) +
+                  (li % kLineRow) * 128);
+    if (p.k_new == nullptr) return;
+    const int pos = kvlen - 1;
+    if (pos < 0 || pos >= p.rope_max) return;
+    const char *kb = static_cast<const char *>(p.k_new) + static_cast<int64_t>(b) * p.ksb * sizeof(T);
+    const char *vb = static_cast<const char *>(p.v_new) + static_cast<int64_t>(b) * p.vsb * sizeof(T);
+    for (int li = lane; li < 2 * HKV * kLineRow; li += 32) {
+      const int which = li / (HKV * kLineRow), r = li % (HKV * kLineRow);
+      const char *base = which ? vb : kb;
+      const int64_t hs = (which ? p.vsh : p.ksh) * sizeof(T);
+      prefetch_l1(base + (r / kLineRow) * hs + (r % kLineRow) * 128);
+    }
+    if (lane < 2 * kLineRow) {
+      const char *tab = static_cast<const char *>(lane < kLineRow ? p.rope_cos : p.rope_sin);
+      prefetch_l1(tab + static_cast<int64_t>(pos) * D * sizeof(T) + (lane % kLineRow) * 128);
+    } else if (lane == 2 * kLineRow) {
+      prefetch_l1(p.indices + ip[b] + pos / p.ps);
+    }
+  };
 
   // =========================== producer warp ==============================
   if (warp == kNC) {
     int k = 0;
     bool ok_run = true;
     const uint64_t policy = evict_first_policy();
-    const int lo = cta * run, hi = min(total, lo + run);
     if (lo < hi) {
       int b = 0;
       {  // request holding global page position lo: last b with indptr[b]-base0 <= lo
@@ -187,7 +287,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       int wbase = lo;
       int pw = pre_pw, pwn = pre_pwn;  // loaded during the prologue
-      pdl_wait();  // the predecessor's K/V writes are visible to the TMA loads
+      // Plain decode: the predecessor may be the append that writes this
+      // step's K/V, so its writes must be visible to the TMA loads first. The
+      // fused form writes the step's K/V itself, and its predecessor must not
+      // write the pool (the entry point's contract): the pages stream while
+      // the predecessor (the previous layer's merge, or a GEMM) still runs.
+      if (p.k_new == nullptr) pdl_wait();
       for (int pos = lo; pos < hi && ok_run;) {
         while (ip[b + 1] - base0 <= pos) ++b;
         const int start_b = ip[b] - base0, end_b = ip[b + 1] - base0;
@@ -230,6 +335,14 @@ __global__ void __launch_bounds__(kThreads, 1)
             const unsigned badl = __ballot_sync(0xffffffffu, bad);
             for (int tt = 0; tt < nt; ++tt) badmask |= ((badl >> (tt * kBoxes)) & 1u) << tt;
           }
+          // A later segment's first stage: the consumers will need the
+          // request's query rows (and, fused, its new K / V rows, the RoPE
+          // rows of its position and the new token's page id) when this
+          // stage comes up, about S stages from now. Pull them into this
+          // SM's L1 now, so that segment start does not stall all consumer
+          // warps on loads queued behind the page stream. (The run's first
+          // segment is loaded by the consumers right away.)
+          if (j0 == 0 && pos != lo) prefetch_segment(b, kvlen);
           // everything but the issue itself is ready before the wait for a free slot
           const int s = k % S;
           const int flags = (j0 == 0 ? 1 : 0) | (j0 + nt >= ntiles ? 2 : 0) | (direct ? 4 : 0) |
@@ -311,6 +424,148 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr int kChunks = D / 8;           // 16-byte chunks of a K or V row
   const int pw_which = lane / kChunks;     // lane -> (K or V, chunk)
   const int pw_cc = lane % kChunks;
+  // this warp's copy of the RoPE cos / sin rows of the segment's position
+  unsigned char *rope_sm = smem + p.rope_off + warp * (2 * D * static_cast<int>(sizeof(T)));
+
+  // Start of a run segment of request b (kv_len tokens; has_new: the
+  // segment holds the request's last token): this warp's query rows into
+  // qa, rotated in the fused form, and the fused append's K / V chunk into
+  // `patch` with the token's page write. Every global load is issued before
+  // any of them is used, so a segment start costs one round trip.
+  auto seg_begin = [&](int b, int kvlen, bool has_new) {
+    const T *qb = static_cast<const T *>(p.q) + static_cast<int64_t>(b) * p.qsb;
+    const int r0 = h * p.group + gid;
+#pragma unroll
+    for (int kk = 0; kk < KS; ++kk) {
+      const int dc = kk * 16 + 2 * tq;
+      uint32_t a0 = 0, a1 = 0, a2 = 0, a3 = 0;
+      if (gid < p.group) {
+        const T *qr = qb + static_cast<int64_t>(r0) * p.qsh;
+        a0 = *reinterpret_cast<const uint32_t *>(qr + dc);
+        a2 = *reinterpret_cast<const uint32_t *>(qr + dc + 8);
+      }
+      if (G16 && gid + 8 < p.group) {
+        const T *qr = qb + static_cast<int64_t>(r0 + 8) * p.qsh;
+        a1 = *reinterpret_cast<const uint32_t *>(qr + dc);
+        a3 = *reinterpret_cast<const uint32_t *>(qr + dc + 8);
+      }
+      qa[kk][0] = a0;
+      qa[kk][1] = a1;
+      qa[kk][2] = a2;
+      qa[kk][3] = a3;
+    }
+    have_patch = false;
+    if (p.k_new == nullptr) return;
+    // fused append: the request's new token is its last, at kv_len - 1
+    const int pos = kvlen - 1;
+    const bool rope_ok = pos >= 0 && pos < p.rope_max;
+    const T *cr = static_cast<const T *>(p.rope_cos) + static_cast<int64_t>(rope_ok ? pos : 0) * D;
+    const T *sr = static_cast<const T *>(p.rope_sin) + static_cast<int64_t>(rope_ok ? pos : 0) * D;
+    // the position's cos and sin rows (D/4 chunks of 16 bytes), staged in
+    // this warp's shared-memory slot below
+    uint4 csv = make_uint4(0, 0, 0, 0);
+    if (rope_ok && lane < D / 4)
+      csv = *reinterpret_cast<const uint4 *>(lane < D / 8 ? cr + lane * 8 : sr + (lane - D / 8) * 8);
+    // the new token's K (rotated) or V chunk of head h: lane -> (K/V, chunk)
+    const bool patch_lane = rope_ok && has_new && lane < 2 * kChunks;
+    const int half = kChunks / 2, pc = pw_cc < half ? pw_cc + half : pw_cc - half;
+    uint4 xv = make_uint4(0, 0, 0, 0), rv = xv;
+    int page = -1;
+    if (patch_lane) {
+      if (pw_which == 0) {
+        const T *kr = static_cast<const T *>(p.k_new) + static_cast<int64_t>(b) * p.ksb +
+                      static_cast<int64_t>(h) * p.ksh;
+        xv = *reinterpret_cast<const uint4 *>(kr + pw_cc * 8);
+        rv = *reinterpret_cast<const uint4 *>(kr + pc * 8);
+      } else {
+        const T *vr = static_cast<const T *>(p.v_new) + static_cast<int64_t>(b) * p.vsb +
+                      static_cast<int64_t>(h) * p.vsh;
+        xv = *reinterpret_cast<const uint4 *>(vr + pw_cc * 8);
+      }
+      if (sw == 0) page = p.indices[ip[b] + pos / p.ps];
+    }
+    // ---- all loads issued; now the arithmetic ----
+    if (!rope_ok) {
+      if (lane == 0) flag(p.status, MI_STATUS_BAD_POSITION);  // left out, q unrotated
+      return;
+    }
+    if (lane < D / 4) *reinterpret_cast<uint4 *>(rope_sm + lane * 16) = csv;
+    __syncwarp();
+    const T *cs_row = reinterpret_cast<const T *>(rope_sm);  // cos [0, D), sin [D, 2D)
+    // all lanes keep the flag, so the stage patch runs warp-wide
+    if (has_new) have_patch = true;
+    if (patch_lane) {
+      if (pw_which == 0) {
+        const uint4 cv = *reinterpret_cast<const uint4 *>(cs_row + pw_cc * 8);
+        const uint4 sv = *reinterpret_cast<const uint4 *>(cs_row + D + pw_cc * 8);
+        const T *xe = reinterpret_cast<const T *>(&xv), *re = reinterpret_cast<const T *>(&rv);
+        const T *ce = reinterpret_cast<const T *>(&cv), *se = reinterpret_cast<const T *>(&sv);
+        T *pe = reinterpret_cast<T *>(&patch);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const float r = Elt<T>::to(re[e]);
+          pe[e] = Elt<T>::from(rope1<T>(Elt<T>::to(xe[e]), pw_cc < half ? -r : r,
+                                        Elt<T>::to(ce[e]), Elt<T>::to(se[e])));
+        }
+      } else {
+        patch = xv;
+      }
+      // one warp per head writes the token into its page slot
+      if (sw == 0 && page >= 0 && page < p.num_pages) {
+        T *dst = static_cast<T *>(p.kv) +
+                 ((static_cast<int64_t>(page) * 2 + pw_which) * p.ps + pos % p.ps) * (HKV * D) +
+                 h * D + pw_cc * 8;
+        *reinterpret_cast<uint4 *>(dst) = patch;
+      }
+    }
+    // q, after the patch (whose registers are free again): element d pairs
+    // with d + D/2, held by this lane in k-step kk + KS/2; a lane's columns
+    // in k-step kk are kk*16 + 2*tq + {0, 8} (+1)
+#pragma unroll
+    for (int kk = 0; kk < KS / 2; ++kk) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int d = kk * 16 + 2 * tq + ((i & 2) ? 8 : 0);
+        const uint32_t cl = *reinterpret_cast<const uint32_t *>(cs_row + d);
+        const uint32_t sl = *reinterpret_cast<const uint32_t *>(cs_row + D + d);
+        const uint32_t ch = *reinterpret_cast<const uint32_t *>(cs_row + d + D / 2);
+        const uint32_t sh = *reinterpret_cast<const uint32_t *>(cs_row + D + d + D / 2);
+        const T *xl = reinterpret_cast<const T *>(&qa[kk][i]);
+        const T *xh = reinterpret_cast<const T *>(&qa[kk + KS / 2][i]);
+        const T *cle = reinterpret_cast<const T *>(&cl);
+        const T *sle = reinterpret_cast<const T *>(&sl);
+        const T *che = reinterpret_cast<const T *>(&ch);
+        const T *she = reinterpret_cast<const T *>(&sh);
+        uint32_t lo, hi;
+        T *loe = reinterpret_cast<T *>(&lo), *hie = reinterpret_cast<T *>(&hi);
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const float x1 = Elt<T>::to(xl[e]), x2 = Elt<T>::to(xh[e]);
+          loe[e] = Elt<T>::from(rope1<T>(x1, -x2, Elt<T>::to(cle[e]), Elt<T>::to(sle[e])));
+          hie[e] = Elt<T>::from(rope1<T>(x2, x1, Elt<T>::to(che[e]), Elt<T>::to(she[e])));
+        }
+        qa[kk][i] = lo;
+        qa[kk + KS / 2][i] = hi;
+      }
+    }
+  };
+
+  // The first segment of this CTA's run is known before its first stage
+  // lands (the producer derives it the same way): its loads go out now,
+  // under the latency of the first TMA loads.
+  int pre_b = -1;
+  {
+    if (lo < hi) {
+      int l = 0, hb = p.batch - 1;
+      while (l < hb) {
+        const int mid = (l + hb + 1) >> 1;
+        if (ip[mid] - base0 <= lo) l = mid; else hb = mid - 1;
+      }
+      while (ip[l + 1] - base0 <= lo) ++l;
+      seg_begin(l, kv_len_of(ip, lp, l, p.ps), ip[l + 1] - base0 <= hi);
+      pre_b = l;
+    }
+  }
 
   for (int k = 0;; ++k) {
     const int s = k % S;
@@ -322,100 +577,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (rec.b < 0) break;
     const int flags = rec.flags;
     if (flags & 1) {  // first tile of a run segment: this warp's query rows
-      const T *qb = static_cast<const T *>(p.q) + static_cast<int64_t>(rec.b) * p.qsb;
-      const int r0 = h * p.group + gid;
-#pragma unroll
-      for (int kk = 0; kk < KS; ++kk) {
-        const int dc = kk * 16 + 2 * tq;
-        uint32_t a0 = 0, a1 = 0, a2 = 0, a3 = 0;
-        if (gid < p.group) {
-          const T *qr = qb + static_cast<int64_t>(r0) * p.qsh;
-          a0 = *reinterpret_cast<const uint32_t *>(qr + dc);
-          a2 = *reinterpret_cast<const uint32_t *>(qr + dc + 8);
-        }
-        if (G16 && gid + 8 < p.group) {
-          const T *qr = qb + static_cast<int64_t>(r0 + 8) * p.qsh;
-          a1 = *reinterpret_cast<const uint32_t *>(qr + dc);
-          a3 = *reinterpret_cast<const uint32_t *>(qr + dc + 8);
-        }
-        qa[kk][0] = a0;
-        qa[kk][1] = a1;
-        qa[kk][2] = a2;
-        qa[kk][3] = a3;
-      }
-      have_patch = false;
-      if (p.k_new != nullptr) {
-        // fused append: the request's new token is its last, at kv_len - 1
-        const int pos = rec.kvlen - 1;
-        if (pos < 0 || pos >= p.rope_max) {
-          if (lane == 0) flag(p.status, MI_STATUS_BAD_POSITION);  // left out, q unrotated
-        } else {
-          const T *cr = static_cast<const T *>(p.rope_cos) + static_cast<int64_t>(pos) * D;
-          const T *sr = static_cast<const T *>(p.rope_sin) + static_cast<int64_t>(pos) * D;
-          // q: element d pairs with d + D/2, held by this lane in k-step kk + KS/2
-#pragma unroll
-          for (int kk = 0; kk < KS / 2; ++kk) {
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              const int d = kk * 16 + 2 * tq + ((i & 2) ? 8 : 0);
-              const uint32_t cl = *reinterpret_cast<const uint32_t *>(cr + d);
-              const uint32_t sl = *reinterpret_cast<const uint32_t *>(sr + d);
-              const uint32_t ch = *reinterpret_cast<const uint32_t *>(cr + d + D / 2);
-              const uint32_t sh = *reinterpret_cast<const uint32_t *>(sr + d + D / 2);
-              const T *xl = reinterpret_cast<const T *>(&qa[kk][i]);
-              const T *xh = reinterpret_cast<const T *>(&qa[kk + KS / 2][i]);
-              const T *cle = reinterpret_cast<const T *>(&cl), *sle = reinterpret_cast<const T *>(&sl);
-              const T *che = reinterpret_cast<const T *>(&ch), *she = reinterpret_cast<const T *>(&sh);
-              uint32_t lo, hi;
-              T *loe = reinterpret_cast<T *>(&lo), *hie = reinterpret_cast<T *>(&hi);
-#pragma unroll
-              for (int e = 0; e < 2; ++e) {
-                const float x1 = Elt<T>::to(xl[e]), x2 = Elt<T>::to(xh[e]);
-                loe[e] = Elt<T>::from(rope1<T>(x1, -x2, Elt<T>::to(cle[e]), Elt<T>::to(sle[e])));
-                hie[e] = Elt<T>::from(rope1<T>(x2, x1, Elt<T>::to(che[e]), Elt<T>::to(she[e])));
-              }
-              qa[kk][i] = lo;
-              qa[kk + KS / 2][i] = hi;
-            }
-          }
-          // this segment holds the new token: lanes build their chunk (all
-          // lanes keep the flag, so the patch below runs warp-wide)
-          if (flags & 8) have_patch = true;
-          if ((flags & 8) && lane < 2 * kChunks) {
-            if (pw_which == 0) {
-              const T *kr = static_cast<const T *>(p.k_new) + static_cast<int64_t>(rec.b) * p.ksb +
-                            static_cast<int64_t>(h) * p.ksh;
-              const int half = kChunks / 2, pc = pw_cc < half ? pw_cc + half : pw_cc - half;
-              const uint4 xv = *reinterpret_cast<const uint4 *>(kr + pw_cc * 8);
-              const uint4 rv = *reinterpret_cast<const uint4 *>(kr + pc * 8);
-              const uint4 cv = *reinterpret_cast<const uint4 *>(cr + pw_cc * 8);
-              const uint4 sv = *reinterpret_cast<const uint4 *>(sr + pw_cc * 8);
-              const T *xe = reinterpret_cast<const T *>(&xv), *re = reinterpret_cast<const T *>(&rv);
-              const T *ce = reinterpret_cast<const T *>(&cv), *se = reinterpret_cast<const T *>(&sv);
-              T *pe = reinterpret_cast<T *>(&patch);
-#pragma unroll
-              for (int e = 0; e < 8; ++e) {
-                const float r = Elt<T>::to(re[e]);
-                pe[e] = Elt<T>::from(rope1<T>(Elt<T>::to(xe[e]), pw_cc < half ? -r : r,
-                                              Elt<T>::to(ce[e]), Elt<T>::to(se[e])));
-              }
-            } else {
-              const T *vr = static_cast<const T *>(p.v_new) + static_cast<int64_t>(rec.b) * p.vsb +
-                            static_cast<int64_t>(h) * p.vsh;
-              patch = *reinterpret_cast<const uint4 *>(vr + pw_cc * 8);
-            }
-            if (sw == 0) {  // one warp per head writes the token into its page slot
-              const int page = p.indices[ip[rec.b] + pos / p.ps];
-              if (page >= 0 && page < p.num_pages) {
-                T *dst = static_cast<T *>(p.kv) +
-                         ((static_cast<int64_t>(page) * 2 + pw_which) * p.ps + pos % p.ps) * (HKV * D) +
-                         h * D + pw_cc * 8;
-                *reinterpret_cast<uint4 *>(dst) = patch;
-              }
-            }
-          }
-        }
-      }
+      if (rec.b != pre_b) seg_begin(rec.b, rec.kvlen, (flags & 8) != 0);
+      pre_b = -1;
 #pragma unroll
       for (int n = 0; n < NT; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
       m0 = m1 = -INFINITY;
@@ -657,13 +820,28 @@ __global__ void __launch_bounds__(64) decode_sk_merge_kernel(const SkParams p, i
   if (wid < p.batch * p.hq) {
     b = wid / p.hq;
     qrow = wid % p.hq;
+  }
+  // the runs that cover request b under the decode kernel's split
+  // (vsplit_run): page j starts at vs_b + c4 + 4 j, run r covers [r R, (r+1) R)
+  {
+    const int bb = wid < p.batch * p.hq ? b : 0;
     const int base0 = p.indptr[0];
-    const int total = p.indptr[p.batch] - base0;
-    const int start_b = p.indptr[b] - base0, end_b = p.indptr[b + 1] - base0;
-    if (total > 0 && end_b > start_b) {
-      const int run = cdiv(total, grid_runs);
-      const int first = start_b / run;
-      nch = (end_b - 1) / run - first + 1;
+    const int np = p.indptr[bb + 1] - p.indptr[bb];
+    int nz_total = 0, nz_before = 0;
+    for (int c0 = 0; c0 < p.batch; c0 += 32) {
+      const int r = c0 + lane;
+      const bool ne = r < p.batch && p.indptr[r + 1] > p.indptr[r];
+      const unsigned m = __ballot_sync(0xffffffffu, ne);
+      nz_total += __popc(m);
+      const int rel = bb - c0;  // requests c0 .. bb-1 of this chunk come before bb
+      nz_before += rel >= 32 ? __popc(m) : (rel > 0 ? __popc(m & ((1u << rel) - 1u)) : 0);
+    }
+    const int vt = 4 * (p.indptr[p.batch] - base0) + p.seg_cost4 * nz_total;
+    if (wid < p.batch * p.hq && vt > 0 && np > 0) {
+      const int rv = vsplit_len(vt, grid_runs);
+      const int v0 = 4 * (p.indptr[bb] - base0) + p.seg_cost4 * nz_before + p.seg_cost4;
+      const int first = v0 / rv;
+      nch = (v0 + 4 * (np - 1)) / rv - first + 1;
       slot0 = first + b;
     }
   }
@@ -717,7 +895,7 @@ __global__ void __launch_bounds__(64) decode_sk_merge_kernel(const SkParams p, i
 // host side: tensor maps (cached per pool), launch
 // ---------------------------------------------------------------------------
 struct SkLayout {
-  int stages, stage_bytes, tps, bar_off, rec_off, scr_off, meta_off, smem;
+  int stages, stage_bytes, tps, bar_off, rec_off, scr_off, meta_off, rope_off, smem;
 };
 
 // Shared memory: stages of tps tiles, barriers (full/empty per stage,
@@ -730,8 +908,9 @@ bool sk_layout(int hkv, int d, int group, int batch, SkLayout *L) {
   const int tile_bytes = 2 * hkv * kTile * d * 2;
   const int scr = kNC * group * (d + 2) * 4;
   const int meta = batch <= kSmemBatch ? ((2 * batch + 4) * 4 + 15) / 16 * 16 : 0;
+  const int rope = kNC * 2 * d * 2;  // cos + sin row per consumer warp (16-bit types)
   const int ctrl = (2 * kMaxStages + 16) * 8 + kMaxStages * 16;
-  const int fixed = 1024 /*align slack*/ + ctrl + scr + meta;
+  const int fixed = 1024 /*align slack*/ + ctrl + scr + meta + rope;
   for (int min_stages = 3; min_stages >= 2; --min_stages) {
     for (int tps = subs; tps >= 1; tps >>= 1) {
       const int stage_bytes = tps * tile_bytes;
@@ -744,8 +923,9 @@ bool sk_layout(int hkv, int d, int group, int batch, SkLayout *L) {
       L->bar_off = st * stage_bytes;
       L->rec_off = L->bar_off + (2 * kMaxStages + 16) * 8;
       L->scr_off = L->rec_off + kMaxStages * 16;
-      L->meta_off = meta ? L->scr_off + scr : -1;
-      L->smem = L->scr_off + scr + meta + 1024;
+      L->rope_off = L->scr_off + scr;
+      L->meta_off = meta ? L->rope_off + rope : -1;
+      L->smem = L->rope_off + rope + meta + 1024;
       return L->smem <= kSmemLimit;
     }
   }
@@ -839,6 +1019,12 @@ int launch_decode_sk(const SkArgs &a) {
   p.rec_off = L.rec_off;
   p.scr_off = L.scr_off;
   p.meta_off = L.meta_off;
+  p.rope_off = L.rope_off;
+  {
+    const double page_bytes = double(a.ps) * a.hkv * a.d * 2 * 2;
+    const double c = 4.0 * kSegCostBytes / page_bytes;
+    p.seg_cost4 = static_cast<int>(c > 4096.0 ? 4096.0 : c + 0.5);
+  }
   if (a.k_new != nullptr) {
     // fused append: 16-byte rows of the new K / V and of the RoPE tables
     const bool rows_ok =

@@ -144,6 +144,11 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t by
       : "memory");
 }
 
+// Non-blocking prefetch of the 128-byte line holding `p` into this SM's L1.
+__device__ __forceinline__ void prefetch_l1(const void *p) {
+  asm volatile("prefetch.global.L1 [%0];" ::"l"(p));
+}
+
 __device__ __forceinline__ void ldsm_x4(uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3,
                                         uint32_t addr) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"

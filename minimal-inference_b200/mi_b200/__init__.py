@@ -11,5 +11,5 @@ raises if it is missing -- there is no CPU fallback.
 
 __all__ = [
     "capi", "page", "decode", "prefill", "kv_cache", "model", "scheduler",
-    "sampling", "rope", "weights",
+    "rope", "weights", "glue", "tp_comm",
 ]

@@ -83,7 +83,12 @@ _SIGS = {
     "mi_silu_mul": ([_c_p, _c_p, _c_i32, _c_i32, _c_i32, _c_p], ctypes.c_int),
     "mi_allreduce_add_rmsnorm": ([_c_p, _c_i64, _c_i64, _c_p, _c_i32, _c_i32, _c_p, _c_p, _c_p,
                                  _c_i32, _c_i32, _c_f, _c_i32, _c_p, _c_p], ctypes.c_int),
+    "mi_set_peer_wait_limit_ns": ([_c_i64], ctypes.c_int),
+    "mi_ipc_export": ([_c_p, _c_p, _c_p], ctypes.c_int),
+    "mi_ipc_open": ([_c_p, _c_p], ctypes.c_int),
+    "mi_ipc_close": ([_c_p], ctypes.c_int),
 }
+IPC_HANDLE_BYTES = 64
 
 _lib = None
 

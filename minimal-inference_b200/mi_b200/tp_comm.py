@@ -1,7 +1,10 @@
 """Fused all-reduce for tensor-parallel decode steps (NVLink peer memory).
 
-``PeerAllReduce`` owns one symmetric buffer per rank (allocated and mapped
-into every rank through torch's symmetric-memory plumbing): a flag array and
+``PeerAllReduce`` owns one symmetric buffer per rank (a plain device
+allocation of the same size on every rank, mapped into every other rank with
+CUDA IPC handles: NVLink P2P mappings, never bound to an NVLink multicast
+object, so a rank that ends cannot leave a multicast object behind that
+other ranks' GPUs still use): a flag array and
 one ``[max_rows, hidden]`` region per call site (two per decoder layer: after
 ``o_proj`` and after ``down_proj``, plus nothing for the final norm, which
 reuses the last ``down_proj`` site). The row-parallel GEMM of a call site
@@ -12,6 +15,8 @@ sharded projections). Calls with more rows than ``max_rows`` (prefill) take
 the NCCL all-reduce instead.
 """
 from __future__ import annotations
+
+import ctypes
 
 import torch
 import torch.distributed as dist
@@ -30,8 +35,6 @@ def _align(n: int, a: int = 256) -> int:
 class PeerAllReduce:
     def __init__(self, group, device, dtype: torch.dtype, hidden: int, num_sites: int,
                  max_rows: int = 64):
-        import torch.distributed._symmetric_memory as symm_mem
-
         if max_rows > MAX_ROWS:
             raise ValueError(f"max_rows {max_rows} > {MAX_ROWS}")
         if hidden % 8:
@@ -46,24 +49,57 @@ class PeerAllReduce:
         self.site_bytes = _align(max_rows * hidden * elt)
         self.data_off0 = _align(self.world * _FLAG_BYTES_PER_RANK)
         total = self.data_off0 + num_sites * self.site_bytes
-        enable = getattr(symm_mem, "enable_symm_mem_for_group", None)
-        if enable is not None:  # required before rendezvous in some torch releases
-            try:
-                enable(group.group_name)
-            except Exception:  # noqa: BLE001 - already enabled / not needed
-                pass
-        self.buf = symm_mem.empty(total, dtype=torch.uint8, device=self.device)
-        self.buf.zero_()
-        self.hdl = symm_mem.rendezvous(self.buf, group)
-        bases = list(self.hdl.buffer_ptrs)
-        off = self.buf.data_ptr() - bases[self.rank]  # same offset in every rank's allocation
-        self.peer_bases = torch.tensor([b + off for b in bases], dtype=torch.int64,
-                                       device=self.device)
+        self.buf = torch.zeros(total, dtype=torch.uint8, device=self.device)
+        self._opened = []       # peer allocations mapped into this process
+        self.peer_bases = None
+        lib = capi.lib()
+        handle = ctypes.create_string_buffer(capi.IPC_HANDLE_BYTES)
+        offset = ctypes.c_int64(0)
+        capi.call("mi_ipc_export", self.buf.data_ptr(), ctypes.addressof(handle),
+                  ctypes.addressof(offset))
+        mine = (bytes(handle.raw), int(offset.value))
+        everyone = [None] * self.world
+        dist.all_gather_object(everyone, mine, group=group)
+        bases = []
+        try:
+            for q, (h, off) in enumerate(everyone):
+                if q == self.rank:
+                    bases.append(self.buf.data_ptr())
+                    continue
+                hb = ctypes.create_string_buffer(h, capi.IPC_HANDLE_BYTES)
+                base = ctypes.c_void_p(0)
+                rc = lib.mi_ipc_open(ctypes.addressof(hb), ctypes.addressof(base))
+                if rc != 0:
+                    raise capi.MiError(f"mi_ipc_open of rank {q}'s buffer failed: "
+                                       f"{lib.mi_last_error().decode(errors='replace')}")
+                self._opened.append(base.value)
+                bases.append(base.value + off)
+        except Exception:
+            self._close_mappings()
+            raise
+        self.peer_bases = torch.tensor(bases, dtype=torch.int64, device=self.device)
         self.counters = torch.zeros(MAX_ROWS, dtype=torch.int32, device=self.device)
         self.status = torch.zeros(1, dtype=torch.int32, device=self.device)
         self.num_sites = num_sites
         torch.cuda.synchronize(self.device)
         dist.barrier(group=group)          # every rank's flags are zero before first use
+
+    def _close_mappings(self) -> None:
+        lib = capi.lib()
+        while self._opened:
+            lib.mi_ipc_close(self._opened.pop())
+
+    def close(self) -> None:
+        """Unmap the peers' buffers once no rank uses them any more (collective:
+        every rank calls it). This rank's own buffer is freed only after every
+        peer has unmapped it."""
+        if self.peer_bases is None:
+            return
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)     # no rank still reads or writes a peer's buffer
+        self._close_mappings()
+        dist.barrier(group=self.group)     # every mapping of this rank's buffer is gone
+        self.peer_bases = None
 
     def usable(self, rows: int) -> bool:
         return 0 < rows <= self.max_rows

@@ -33,6 +33,14 @@ run on the CPU. Four fixtures come out:
     reference ``Scheduler`` on CPU. Stores the generated tokens (the teacher
     sequence for the GPU run), per-step logit digests and per-layer KV digests
     taken just before each request's cache slot is released.
+``config1_bf16.npz``
+    The same run with the model (weights, RoPE tables, cache) in bf16 and 8
+    greedy decode steps: the reference's bf16 numbers for a model-level GPU
+    run whose decode steps go through the fused append + decode kernel
+    (bf16 only; the fp32 run takes the two-call path). Also stores the
+    reference's own bf16 logit noise floor (``bf16_logit_noise_floor``): how
+    far its logits move when only the GEMM accumulation changes, the scale
+    below which a bf16 comparison of 24 layers cannot resolve anything.
 """
 from __future__ import annotations
 
@@ -62,6 +70,7 @@ CONFIG1 = dict(
 CONFIG1_SEED = 20240601
 CONFIG1_PROMPTS = [37, 128, 255, 500]
 CONFIG1_DECODE_STEPS = 50
+CONFIG1_BF16_DECODE_STEPS = 8
 LOGIT_SAMPLE_IDS = 128
 KV_SAMPLES = 48
 
@@ -294,7 +303,39 @@ def _digest_rows(logits: np.ndarray, sample_ids: np.ndarray) -> dict:
             "lse": lse.astype(np.float32), "sampled": logits[:, sample_ids].astype(np.float32)}
 
 
-def gen_config1(ref_model, ref_sched) -> dict:
+def bf16_logit_noise_floor(model, prompts, generated) -> float:
+    """How far the reference's own bf16 logits move when only the GEMM
+    accumulation changes: every request's teacher-forced sequence (prompt +
+    generated tokens) through the reference model twice, with its stock bf16
+    ``F.linear`` and with each linear computed in fp32 and rounded to bf16
+    once; the largest difference over the positions that produced a token."""
+    import torch.nn.functional as F
+
+    def run():
+        rows = []
+        with torch.no_grad():
+            for ids, toks in zip(prompts, generated):
+                seq = torch.tensor(list(ids) + list(toks[:-1])).unsqueeze(0)
+                lg = model(seq, position_ids=torch.arange(seq.shape[1]).unsqueeze(0))[0]
+                rows.append(lg[len(ids) - 1:].float())
+        return rows
+
+    stock = run()
+    orig = F.linear
+
+    def linear_fp32(x, w, b=None):
+        return orig(x.float(), w.float(), None if b is None else b.float()).to(x.dtype)
+
+    F.linear = linear_fp32
+    try:
+        fp32acc = run()
+    finally:
+        F.linear = orig
+    return max(float((a - b).abs().max()) for a, b in zip(stock, fp32acc))
+
+
+def gen_config1(ref_model, ref_sched, dtype=torch.float32,
+                decode_steps: int = CONFIG1_DECODE_STEPS) -> dict:
     from mi_b200.weights import init_random_weights
 
     torch.set_num_threads(os.cpu_count() or 8)
@@ -302,9 +343,9 @@ def gen_config1(ref_model, ref_sched) -> dict:
     model = ref_model.Model(cfg)
     t0 = time.time()
     init_random_weights(model, CONFIG1_SEED)
-    model.eval()
-    print(f"config1: weights in {time.time() - t0:.1f}s", flush=True)
-    sched = ref_sched.Scheduler(model, cfg, torch.device("cpu"), torch.float32,
+    model = model.to(dtype).eval()
+    print(f"config1 ({dtype}): weights in {time.time() - t0:.1f}s", flush=True)
+    sched = ref_sched.Scheduler(model, cfg, torch.device("cpu"), dtype,
                                 max_batch_size=4, max_seq_len=4096, page_size=16,
                                 eos_token_ids=set(), use_flashinfer=True)
     assert not sched.use_flashinfer
@@ -348,7 +389,7 @@ def gen_config1(ref_model, ref_sched) -> dict:
 
     sched.kv_cache.release_slot = release_slot
     for i, ids in enumerate(prompts):
-        r = ref_sched.Request(f"r{i}", ids, CONFIG1_DECODE_STEPS + 1, 0.0)
+        r = ref_sched.Request(f"r{i}", ids, decode_steps + 1, 0.0)
         reqs.append(r)
         sched.submit_request(r)
     order = []
@@ -386,6 +427,14 @@ def gen_config1(ref_model, ref_sched) -> dict:
     out["logit_labels"] = np.asarray(labels, np.int32)
     out["sample_ids"] = sample_ids.astype(np.int32)
     out["seed"] = np.asarray([CONFIG1_SEED], np.int64)
+    out["dtype"] = np.asarray([str(dtype).removeprefix("torch.")])
+    if dtype == torch.bfloat16:
+        model.forward = orig_forward
+        floor = bf16_logit_noise_floor(model, [r.input_ids for r in reqs],
+                                       [r.generated_tokens for r in reqs])
+        print(f"config1 ({dtype}): logit noise floor of the reference itself {floor:.4f}",
+              flush=True)
+        out["logit_noise_floor"] = np.asarray([floor], np.float32)
     out["prompt_lens"] = np.asarray(CONFIG1_PROMPTS, np.int32)
     for i, r in enumerate(reqs):
         out[f"prompt_{i}"] = np.asarray(r.input_ids, np.int32)
@@ -399,7 +448,7 @@ def gen_config1(ref_model, ref_sched) -> dict:
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, help="reference checkout (model.py, scheduler.py)")
-    ap.add_argument("--only", default="rope,attn,sched,config1")
+    ap.add_argument("--only", default="rope,attn,sched,config1,config1_bf16")
     args = ap.parse_args()
     sys.path.insert(0, os.path.abspath(args.reference))
     import model as ref_model  # noqa: E402
@@ -415,6 +464,10 @@ def main() -> None:
             json.dump(gen_sched_trace(ref_model, ref_sched), f, separators=(",", ":"))
     if "config1" in only:
         np.savez_compressed(os.path.join(HERE, "config1.npz"), **gen_config1(ref_model, ref_sched))
+    if "config1_bf16" in only:
+        np.savez_compressed(os.path.join(HERE, "config1_bf16.npz"),
+                            **gen_config1(ref_model, ref_sched, torch.bfloat16,
+                                          CONFIG1_BF16_DECODE_STEPS))
     for fn in sorted(os.listdir(HERE)):
         if fn.endswith((".npz", ".json")):
             print(fn, os.path.getsize(os.path.join(HERE, fn)))

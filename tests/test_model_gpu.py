@@ -4,7 +4,10 @@
   package's Scheduler, teacher-forced with the token sequence the reference
   generated on CPU (tests/golden/config1.npz): per-step logit digests and
   per-layer KV samples must match the reference within 2e-2, and every page
-  must come back to the pool.
+  must come back to the pool. The same in bf16 (tests/golden/config1_bf16.npz,
+  8 decode steps), where the decode steps run the fused append + decode
+  kernel; its logit bar is the reference's own bf16 noise floor when that is
+  above 2e-2.
 * A Mistral-7B-shaped model (2 layers, bf16): CUDA-graph decode steps agree
   with eager decode steps, padding lanes included.
 """
@@ -26,18 +29,23 @@ def _config1():
     return PRESETS["qwen2.5-0.5b"]
 
 
-def test_config1_parity_with_reference_teacher_forced():
+@pytest.mark.parametrize("fixture,dtype", [("config1.npz", torch.float32),
+                                           ("config1_bf16.npz", torch.bfloat16)])
+def test_config1_parity_with_reference_teacher_forced(fixture, dtype):
+    """fp32: the reference's own CPU precision for config 1 (decode steps take
+    the append + decode calls). bf16: the reference run in bf16, whose decode
+    steps here go through the fused append + decode kernel."""
     from mi_b200.model import Model
     from mi_b200.scheduler import Request, Scheduler
     from mi_b200.weights import init_random_weights
-    fx = np.load(os.path.join(GOLDEN, "config1.npz"))
+    fx = np.load(os.path.join(GOLDEN, fixture))
     cfg = _config1()
     model = Model(cfg)
     init_random_weights(model, int(fx["seed"][0]))
-    model = model.to(device=DEV, dtype=torch.float32).eval().prepare()
+    model = model.to(device=DEV, dtype=dtype).eval().prepare()
     n_req = len(fx["prompt_lens"])
     teacher = {f"r{i}": fx[f"tokens_{i}"].tolist() for i in range(n_req)}
-    sched = Scheduler(model, cfg, torch.device(DEV), torch.float32, max_batch_size=4,
+    sched = Scheduler(model, cfg, torch.device(DEV), dtype, max_batch_size=4,
                       max_seq_len=4096, page_size=16, eos_token_ids=set(),
                       teacher_tokens=teacher)
     sched.record_logits = True
@@ -87,6 +95,10 @@ def test_config1_parity_with_reference_teacher_forced():
     labels = [tuple(int(x) for x in lab) for lab in fx["logit_labels"]]
     assert set(labels) == set(mine)
     sample_ids = fx["sample_ids"]
+    # fp32: 2e-2. bf16: no further from the reference than the reference's
+    # own bf16 logits move when only its GEMM accumulation changes (stored by
+    # the fixture generator; 24 bf16 layers put that above 2e-2)
+    tol = max(2e-2, float(fx["logit_noise_floor"][0])) if "logit_noise_floor" in fx else 2e-2
     worst = 0.0
     argmax_match = 0
     for k, lab in enumerate(labels):
@@ -97,9 +109,18 @@ def test_config1_parity_with_reference_teacher_forced():
         m = row.max()
         lse = float(np.log(np.exp(row - m).sum()) + m)
         worst = max(worst, abs(lse - float(fx["logit_lse"][k])))
-        argmax_match += int(row.argmax() == fx["logit_argmax"][k])
-    assert worst <= 2e-2, f"max logit deviation {worst}"
-    assert argmax_match >= 0.95 * len(labels)
+        a = int(row.argmax())
+        if a == int(fx["logit_argmax"][k]):
+            argmax_match += 1
+        elif "logit_noise_floor" in fx and a in top:
+            # bf16: a near-tie of the reference's best token counts as a match
+            near = fx["logit_top_vals"][k][list(top).index(a)] >= fx["logit_top_vals"][k][0] - tol
+            argmax_match += int(near)
+    assert worst <= tol, f"max logit deviation {worst} > {tol}"
+    if "logit_noise_floor" in fx:
+        assert argmax_match == len(labels)         # every row's pick is the best or a near-tie
+    else:
+        assert argmax_match >= 0.95 * len(labels)
     # KV pages vs the reference's padded cache, sampled
     for i in range(n_req):
         ks, vs, n = kv_samples[i]

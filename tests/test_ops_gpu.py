@@ -304,6 +304,77 @@ def test_decode_append_matches_append_then_decode(hq, hkv, d, ps):
     assert torch.equal(oa.view(torch.int16), ob.view(torch.int16))
 
 
+def _assert_pool_bits(pool: torch.Tensor, want: np.ndarray, dtype: str, block: int = 512):
+    """Every page of the device pool equals the oracle's, bit for bit (in
+    blocks of pages, to bound host memory at full size)."""
+    for p0 in range(0, want.shape[0], block):
+        got = bits(pool[p0:p0 + block])
+        exp = oracle_bits(want[p0:p0 + block], dtype)
+        if not np.array_equal(got, exp):
+            bad = np.argwhere(got != exp)[0]
+            raise AssertionError(f"page {p0 + bad[0]} differs from the oracle at {tuple(bad)}")
+
+
+def _fused_step_vs_oracle(seed, lens, hq, hkv, d, ps, dtype, num_pages=None):
+    """The fused decode step (run_with_append) against the oracle's RoPE
+    append (model.py:169-170, :207-216) followed by its paged decode
+    (model.py:235): pages bit-exact, output within the dtype's tolerance."""
+    from mi_b200.decode import BatchDecodeWithPagedKVCacheWrapper
+    from mi_b200.rope import rope_tables
+    c = paged_case(seed, lens, hq, hkv, d, page_size=ps, dtype=dtype, num_pages=num_pages)
+    rng = np.random.default_rng(seed + 7)
+    b = len(lens)
+    raw = lambda h: po.round_to(rng.standard_normal((b, h, d), dtype=np.float32), dtype)  # noqa: E731
+    q, k, v = raw(hq), raw(hkv), raw(hkv)
+    cos, sin = rope_tables(d, 8192, 1e6, tdt(dtype))
+    cos_h, sin_h = cos.float().numpy(), sin.float().numpy()
+    pos = np.asarray(lens, np.int64) - 1          # each request's new token is its last
+    want_pool = c["pool"]                           # updated in place by the oracle below
+    pool = to_dev(want_pool, dtype)
+    po.append_paged_kv_rope(want_pool, k, v, np.arange(b), pos, c["indices"], c["indptr"], ps,
+                            cos_h, sin_h, dtype)
+    q_rot = po.apply_rope(q, cos_h[pos][:, None, :], sin_h[pos][:, None, :], dtype)
+    want_out, _ = po.decode_attention(q_rot, want_pool, c["indptr"], c["indices"], c["last"], ps)
+
+    w = BatchDecodeWithPagedKVCacheWrapper(torch.zeros(64 << 20, dtype=torch.uint8, device=DEV))
+    w.plan(i32(c["indptr"]), i32(c["indices"]), i32(c["last"]), hq, hkv, d, ps,
+           q_data_type=tdt(dtype))
+    out = w.run_with_append(to_dev(q, dtype), pool, to_dev(k, dtype), to_dev(v, dtype),
+                            cos.to(DEV), sin.to(DEV))
+    torch.cuda.synchronize()
+    w.check_status()
+    _assert_pool_bits(pool, want_pool, dtype)
+    err = float(np.abs(f32(out) - want_out).max())
+    assert err <= TOL[dtype], err
+
+
+# new tokens at slot 0 (len % 16 == 1) and at the last slot of a 16-token page
+# (len % 16 == 0), one-token requests, and contexts long enough to be cut
+# across stream-K runs next to ones wholly inside a run
+FUSED_LENS = [1, 16, 17, 300, 1024, 33, 4000, 129, 2, 640, 48, 4097]
+
+
+@pytest.mark.parametrize("dtype", ["bfloat16", "float16"])
+@pytest.mark.parametrize("ps", [8, 16, 32])
+@pytest.mark.parametrize("hq,hkv,d", [(32, 8, 128), (28, 4, 128)])
+def test_decode_append_matches_oracle(dtype, ps, hq, hkv, d):
+    """Groups 4 and 7 at head_dim 128, page sizes 8 (outside the fused
+    kernel: the two calls), 16 and 32, bf16 and fp16."""
+    _fused_step_vs_oracle(70 + ps, FUSED_LENS, hq, hkv, d, ps, dtype)
+
+
+@pytest.mark.parametrize("dtype", ["bfloat16", "float16"])
+@pytest.mark.parametrize("hq,hkv,d", [(8, 1, 64), (14, 2, 64), (16, 1, 128), (64, 8, 128)])
+def test_decode_append_matches_oracle_other_heads(dtype, hq, hkv, d):
+    _fused_step_vs_oracle(90 + hq, FUSED_LENS[:9], hq, hkv, d, 16, dtype)
+
+
+def test_decode_append_config2_full_size_matches_oracle():
+    """BASELINE config 2 at full size: B=32, ctx U[256,4096], random tables
+    in a 10240-page pool, bf16; the kernel the bench times."""
+    _fused_step_vs_oracle(0, config2_lens(0), 32, 8, 128, 16, "bfloat16", num_pages=10240)
+
+
 def test_decode_append_outside_the_fused_kernel_takes_the_two_calls():
     """fp32 is outside the fused kernel: run_with_append makes the append and
     decode calls itself, with the same result."""

@@ -126,6 +126,47 @@ def tp_gpu_peer_vs_nccl(rank: int, world: int, init_file: str, prompts, max_new,
         toks_b, logs_b = run_scheduler_logits(model, cfg, dev, prompts, max_new, teacher=toks_a)
         torch.cuda.synchronize()
         model.comm.check_status()
+        model.comm.close()
         out_q.put((rank, toks_a, logs_a, toks_b, logs_b))
     finally:
         dist.destroy_process_group()
+
+
+# ---------------------------------------------------------------------------
+# GPU: IPC mapping between two processes on one GPU
+# ---------------------------------------------------------------------------
+class _Cai:
+    """A raw device pointer as a torch-readable array (``__cuda_array_interface__``)."""
+
+    def __init__(self, ptr, n):
+        self.__cuda_array_interface__ = {"shape": (n,), "typestr": "|u1",
+                                         "data": (ptr, False), "version": 3}
+
+
+def ipc_child(handle: bytes, offset: int, n: int, q) -> None:
+    """Child of the one-GPU IPC test: map the parent's buffer, read its first
+    half, write a pattern into its second half, unmap."""
+    import ctypes
+
+    import torch as t
+    from mi_b200 import capi
+
+    try:
+        t.cuda.set_device(0)
+        t.zeros(1, device="cuda")                     # context up before the mapping
+        lib = capi.lib()
+        hb = ctypes.create_string_buffer(handle, capi.IPC_HANDLE_BYTES)
+        base = ctypes.c_void_p(0)
+        rc = lib.mi_ipc_open(ctypes.addressof(hb), ctypes.addressof(base))
+        if rc != 0:
+            q.put(("error", lib.mi_last_error().decode()))
+            return
+        view = t.as_tensor(_Cai(base.value + offset, n), device="cuda")
+        seen = view[: n // 2].cpu().numpy().tobytes()
+        view[n // 2:].copy_(t.arange(n - n // 2, device="cuda").to(t.uint8) ^ 0x5A)
+        t.cuda.synchronize()
+        del view
+        rc = lib.mi_ipc_close(base)
+        q.put(("ok", seen, rc))
+    except Exception as e:  # noqa: BLE001 - reported to the parent
+        q.put(("error", repr(e)))
