@@ -38,8 +38,8 @@ run on the CPU. Four fixtures come out:
     greedy decode steps: the reference's bf16 numbers for a model-level GPU
     run whose decode steps go through the fused append + decode kernel
     (bf16 only; the fp32 run takes the two-call path). Also stores the
-    reference's own bf16 logit noise floor (``bf16_logit_noise_floor``): how
-    far its logits move when only the GEMM accumulation changes, the scale
+    reference's own bf16 noise floor (``bf16_noise_floor``): how far its
+    logits and K / V move when only the GEMM accumulation changes, the scale
     below which a bf16 comparison of 24 layers cannot resolve anything.
 """
 from __future__ import annotations
@@ -303,24 +303,31 @@ def _digest_rows(logits: np.ndarray, sample_ids: np.ndarray) -> dict:
             "lse": lse.astype(np.float32), "sampled": logits[:, sample_ids].astype(np.float32)}
 
 
-def bf16_logit_noise_floor(model, prompts, generated) -> float:
-    """How far the reference's own bf16 logits move when only the GEMM
+def bf16_noise_floor(model, prompts, generated) -> tuple[float, float]:
+    """How far the reference's own bf16 numbers move when only the GEMM
     accumulation changes: every request's teacher-forced sequence (prompt +
     generated tokens) through the reference model twice, with its stock bf16
     ``F.linear`` and with each linear computed in fp32 and rounded to bf16
-    once; the largest difference over the positions that produced a token."""
+    once. Returns the largest logit difference over the positions that
+    produced a token, and the largest difference of any layer's K / V
+    projection output (what the cache stores, before RoPE on K)."""
     import torch.nn.functional as F
+
+    kv_out = []
+    hooks = [m.register_forward_hook(lambda _m, _i, o: kv_out.append(o.float()))
+             for layer in model.layers for m in (layer.self_attn.k_proj, layer.self_attn.v_proj)]
 
     def run():
         rows = []
+        kv_out.clear()
         with torch.no_grad():
             for ids, toks in zip(prompts, generated):
                 seq = torch.tensor(list(ids) + list(toks[:-1])).unsqueeze(0)
                 lg = model(seq, position_ids=torch.arange(seq.shape[1]).unsqueeze(0))[0]
                 rows.append(lg[len(ids) - 1:].float())
-        return rows
+        return rows, list(kv_out)
 
-    stock = run()
+    stock, kv_stock = run()
     orig = F.linear
 
     def linear_fp32(x, w, b=None):
@@ -328,10 +335,14 @@ def bf16_logit_noise_floor(model, prompts, generated) -> float:
 
     F.linear = linear_fp32
     try:
-        fp32acc = run()
+        fp32acc, kv_fp32 = run()
     finally:
         F.linear = orig
-    return max(float((a - b).abs().max()) for a, b in zip(stock, fp32acc))
+        for h in hooks:
+            h.remove()
+    logit = max(float((a - b).abs().max()) for a, b in zip(stock, fp32acc))
+    kv = max(float((a - b).abs().max()) for a, b in zip(kv_stock, kv_fp32))
+    return logit, kv
 
 
 def gen_config1(ref_model, ref_sched, dtype=torch.float32,
@@ -430,11 +441,12 @@ def gen_config1(ref_model, ref_sched, dtype=torch.float32,
     out["dtype"] = np.asarray([str(dtype).removeprefix("torch.")])
     if dtype == torch.bfloat16:
         model.forward = orig_forward
-        floor = bf16_logit_noise_floor(model, [r.input_ids for r in reqs],
-                                       [r.generated_tokens for r in reqs])
-        print(f"config1 ({dtype}): logit noise floor of the reference itself {floor:.4f}",
-              flush=True)
+        floor, kv_floor = bf16_noise_floor(model, [r.input_ids for r in reqs],
+                                           [r.generated_tokens for r in reqs])
+        print(f"config1 ({dtype}): noise floor of the reference itself: logits {floor:.4f}, "
+              f"K/V {kv_floor:.4f}", flush=True)
         out["logit_noise_floor"] = np.asarray([floor], np.float32)
+        out["kv_noise_floor"] = np.asarray([kv_floor], np.float32)
     out["prompt_lens"] = np.asarray(CONFIG1_PROMPTS, np.int32)
     for i, r in enumerate(reqs):
         out[f"prompt_{i}"] = np.asarray(r.input_ids, np.int32)

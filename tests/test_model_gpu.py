@@ -125,8 +125,9 @@ def test_config1_parity_with_reference_teacher_forced(fixture, dtype):
     for i in range(n_req):
         ks, vs, n = kv_samples[i]
         assert n == int(fx[f"kv_{i}_len"])
-        np.testing.assert_allclose(ks, fx[f"kv_{i}_k"], atol=2e-2, rtol=0)
-        np.testing.assert_allclose(vs, fx[f"kv_{i}_v"], atol=2e-2, rtol=0)
+        kv_tol = max(2e-2, float(fx["kv_noise_floor"][0])) if "kv_noise_floor" in fx else 2e-2
+        np.testing.assert_allclose(ks, fx[f"kv_{i}_k"], atol=kv_tol, rtol=0)
+        np.testing.assert_allclose(vs, fx[f"kv_{i}_v"], atol=kv_tol, rtol=0)
     # all pages back in the pool
     assert int(sched.kv_cache.pool_ctrl[1].item()) == sched.kv_cache.max_num_pages - 1
     assert sched.kv_cache.num_free_pages == sched.kv_cache.max_num_pages - 1
