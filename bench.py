@@ -19,8 +19,16 @@ the timed region.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-N > 1 runs under torchrun, one rank per GPU, each rank an independent
-replica of the workload (weak scaling; attention needs no collective).
+N > 1 runs under torchrun, one rank per GPU. The headline is config 2 split
+by KV head: every GPU holds 8/N of the KV heads of every page and decodes
+them with their query heads (strong scaling; attention needs no exchange
+between heads). Beside it: ``replicas`` (every GPU runs the whole step on its
+own pools: weak scaling, no collective) and ``tp_decode`` (
+Qwen2.5-72B-shape decode at batch 64, tensor parallel over the N GPUs, with
+the decode all-reduce named). N = 1 adds the reference's CPU path
+(``cpu_baseline``), the Mistral-7B-shape decode (config 3), the prefill
+kernel on config 3's prompts, Qwen2.5-7B serving under churn (config 4) and
+config 1's decode step beside the reference's CPU step.
 """
 from __future__ import annotations
 
@@ -247,26 +255,24 @@ def churn_requests(n, vocab, seed=11, p_lo=64, p_hi=2048, o_lo=16, o_hi=512):
              int(rng.integers(o_lo, o_hi + 1))) for _ in range(n)]
 
 
-def run_churn(args):
+def churn_measure(dev, n_req=160, name=None) -> dict:
     """Qwen2.5-7B-shape serving under churn.
 
     max_batch 48, max_seq 4096, page_size 16; 48 requests start, and a new
     one (prompt U[64,2048], output U[16,512], seeded) is submitted whenever
-    one finishes, until ``--batch`` requests (default 160) have been served,
-    so admissions, prefills, page growth and retirements interleave and the
-    pool fragments. Random bf16 weights, greedy, EOS disabled (outputs run to
-    their drawn length). Reports generated tokens per second of the whole
-    run, the reference-definition T2T and TTFT, and the decode step time.
+    one finishes, until ``n_req`` requests have been served, so admissions,
+    prefills, page growth and retirements interleave and the pool fragments.
+    Random bf16 weights, greedy, EOS disabled (outputs run to their drawn
+    length). Reports generated tokens per second of the whole run, the
+    reference-definition T2T and TTFT, the decode step time, and whether
+    every page came back to the pool.
     """
     import torch
     from mi_b200.model import PRESETS, Model
     from mi_b200.scheduler import Request, Scheduler
 
-    dev = torch.device("cuda", dist_env()[2])
-    torch.cuda.set_device(dev)
-    name = args.model or "qwen2.5-7b"
+    name = name or "qwen2.5-7b"
     cfg = PRESETS[name]
-    n_req = args.batch or 160
     model = Model.create(cfg, dev, torch.bfloat16, seed=7)
     sched = Scheduler(model, cfg, dev, torch.bfloat16, max_batch_size=48, max_seq_len=4096,
                       page_size=16, eos_token_ids=set())
@@ -292,7 +298,7 @@ def run_churn(args):
             sched.submit_request(r)
             nxt += 1
 
-    clocks = ClockSampler(dist_env()[2])
+    clocks = ClockSampler(dev.index or 0)
     t0 = time.perf_counter()
     submit(48)
     steps, step_ms, min_free = 0, [], sched.kv_cache.num_free_pages
@@ -315,59 +321,77 @@ def run_churn(args):
     ttft = [r.prefill_done_time - r.submit_time for r in reqs]
     complete = all(len(r.generated_tokens) == stream[i][1] for i, r in enumerate(reqs))
     pages_back = int(sched.kv_cache.pool_ctrl[1].item()) == sched.kv_cache.max_num_pages - 1
+    pool_pages = sched.kv_cache.max_num_pages
     sched.close()
-    line = {"metric": f"{name} serving under churn: generated tok/s (config 4)",
-            "value": round(gen / wall, 1), "unit": "tok/s", "n_gpus": 1, "steps": steps,
-            "warmup": len(warm), "ms_per_step": round(statistics.median(step_ms), 3),
-            "higher_is_better": True, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": "continuous batching with a new request whenever one "
-                                   "finishes", "model": name, "max_batch": 48,
-                       "max_seq_len": 4096, "requests": n_req,
-                       "prompt_lens": "U[64,2048]", "output_lens": "U[16,512]",
-                       "page_size": 16, "weights": "random N(0,0.02) bf16"},
+    del sched, model
+    torch.cuda.empty_cache()
+    return {"metric": f"{name} serving under churn: generated tok/s (config 4)",
+            "value": round(gen / wall, 1), "unit": "tok/s", "steps": steps,
+            "warmup_requests": len(warm),
+            "decode_step_ms_median": round(statistics.median(step_ms), 3),
+            "model": name, "max_batch": 48, "max_seq_len": 4096, "requests": n_req,
+            "prompt_lens": "U[64,2048] seeded", "output_lens": "U[16,512] seeded",
+            "page_size": 16, "weights": "random N(0,0.02) bf16",
             "t2t_ms_mean": round(statistics.mean(t2t) * 1e3, 3),
             "ttft_ms_mean": round(statistics.mean(ttft) * 1e3, 1),
             "generated_tokens": gen, "wall_s": round(wall, 3),
-            "min_free_pages": min_free, "pool_pages": sched.kv_cache.max_num_pages,
+            "min_free_pages": min_free, "pool_pages": pool_pages,
             "all_outputs_complete": complete, "all_pages_returned": pages_back,
             "clocks": clk}
+
+
+def run_churn(args):
+    """``--workload config4``: ``churn_measure`` on its own (``--batch``
+    requests, default 160)."""
+    import torch
+    dev = torch.device("cuda", dist_env()[2])
+    torch.cuda.set_device(dev)
+    r = churn_measure(dev, n_req=args.batch or 160, name=args.model)
+    line = {"metric": r["metric"], "value": r["value"], "unit": "tok/s", "n_gpus": 1,
+            "steps": r["steps"], "warmup": r["warmup_requests"],
+            "ms_per_step": r["decode_step_ms_median"], "higher_is_better": True,
+            "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "continuous batching with a new request whenever one "
+                                   "finishes", "model": r["model"], "max_batch": 48,
+                       "max_seq_len": 4096, "requests": r["requests"],
+                       "prompt_lens": r["prompt_lens"], "output_lens": r["output_lens"],
+                       "page_size": 16, "weights": r["weights"]},
+            **{k: r[k] for k in ("t2t_ms_mean", "ttft_ms_mean", "generated_tokens", "wall_s",
+                                 "min_free_pages", "pool_pages", "all_outputs_complete",
+                                 "all_pages_returned", "clocks")}}
     print(json.dumps(line), flush=True)
 
 
 # ---------------------------------------------------------------------------
-def run_tp_decode(args):
+def tp_decode(args, rank, world, local, dev, batch=64, steps=128, allreduce=None,
+              name=None) -> dict:
     """Qwen2.5-72B-shape continuous-batching decode with
-    tensor parallelism over the N GPUs of the launch (one rank per GPU, NCCL).
+    tensor parallelism over the ranks of the (already initialised) process
+    group, one rank per GPU.
 
-    64 requests, prompts U[512, 4096] of random ids (seeded, the same on every
-    rank), 129 output tokens each (1 from prefill + 128 decode steps), page
-    size 16, max_seq_len 4224, greedy sampling, CUDA-graph decode with the two
-    all-reduces per layer captured in the graph. Random bf16 weights
-    (``Model.create``: each rank keeps its slices of the same seeded tensors).
-    T2T follows the reference's definition (per request, time between its
-    first and last token over tokens - 1, averaged); every timing is the max
-    over ranks. ``--model`` swaps in a smaller preset for quick checks.
+    ``batch`` requests, prompts U[512, 4096] of random ids (seeded, the same on
+    every rank), ``steps + 1`` output tokens each (1 from prefill), page size
+    16, greedy sampling, CUDA-graph decode with the two all-reduces per layer
+    captured in the graph. Random bf16 weights (``Model.create``: each rank
+    keeps its slices of the same seeded tensors). T2T follows the reference's
+    definition (per request, time between its first and last token over
+    tokens - 1, averaged); every timing is the max over ranks. Returns the
+    measured numbers (every rank; the same on all).
     """
     import torch
     import torch.distributed as dist
-    from datetime import timedelta
 
     from mi_b200.model import PRESETS, Model
     from mi_b200.scheduler import Request, Scheduler
 
-    rank, world, local = dist_env()
-    dev = torch.device("cuda", local)
-    torch.cuda.set_device(dev)
-    if world > 1:
-        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
     group = dist.group.WORLD if world > 1 else None
-    name = args.model or "qwen2.5-72b"
+    name = name or "qwen2.5-72b"
     cfg = PRESETS[name]
-    batch, lo, hi, steps = args.batch or 64, 512, 4096, args.decode_steps or 128
+    lo, hi = 512, 4096
     t0 = time.perf_counter()
     model = Model.create(cfg, dev, torch.bfloat16, seed=5, tp_rank=rank, tp_size=world,
                          tp_group=group)
-    allreduce = args.allreduce
+    allreduce = allreduce or "auto"
     if allreduce == "auto":
         allreduce = "peer" if world <= 4 else "nccl"
     if world > 1 and allreduce == "peer":
@@ -421,28 +445,54 @@ def run_tp_decode(args):
         model.comm.check_status()
         model.comm.close()
     del sched, model
+    torch.cuda.empty_cache()
+    return {"metric": f"{name} decode tok/s @B={batch}, tensor parallel (config 5)",
+            "value": round(batch / (dec_ms / 1e3), 1), "unit": "tok/s",
+            "decode_step_ms": round(dec_ms, 3), "t2t_ms": round(t2t, 3),
+            "t2t_tok_s": round(batch / (t2t / 1e3), 1),
+            "t2t_note": ("reference definition (per request, first to last token): includes "
+                         "the wait of early-prefilled requests for the later prefill chunks"),
+            "parallelism": f"tp{world}", "decode_allreduce": allreduce if world > 1 else "none",
+            "model": name, "batch": batch, "decode_steps": steps,
+            "prompt_lens": f"U[{lo},{hi}] seeded", "weights": "random N(0,0.02) bf16",
+            "first_step_s (prefill of all + 1 decode)": round(first_s, 3),
+            "model_init_s": round(init_s, 2), "graph_capture_s": round(capture_s, 2),
+            "decode_steps_timed": n_dec, "all_requests_complete": ok, "clocks": clk}
+
+
+def run_tp_decode(args):
+    """``--workload config5``: ``tp_decode`` at the launch's N on its own."""
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    rank, world, local = dist_env()
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+    batch, steps = args.batch or 64, args.decode_steps or 128
+    r = tp_decode(args, rank, world, local, dev, batch=batch, steps=steps,
+                  allreduce=args.allreduce, name=args.model)
     if world > 1:
         dist.destroy_process_group()
     if rank != 0:
         return
     line = {
-        "metric": f"{name} decode tok/s @B={batch}, tensor parallel (config 5)",
-        "value": round(batch / (t2t / 1e3), 1), "unit": "tok/s", "n_gpus": world,
-        "steps": steps, "warmup": 0, "ms_per_step": round(dec_ms, 3), "t2t_ms": round(t2t, 3),
-        "decode_step_tok_s": round(batch / (dec_ms / 1e3), 1),
-        "t2t_note": ("reference definition (per request, first to last token): includes the "
-                     "wait of early-prefilled requests for the later prefill chunks"),
+        "metric": r["metric"], "value": r["t2t_tok_s"], "unit": "tok/s", "n_gpus": world,
+        "steps": steps, "warmup": 0, "ms_per_step": r["decode_step_ms"], "t2t_ms": r["t2t_ms"],
+        "decode_step_tok_s": r["value"], "t2t_note": r["t2t_note"],
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic",
         "config": {"workload": "BASELINE config 5: continuous-batching decode, all requests "
-                               "admitted at once, greedy", "model": name,
-                   "global_batch": batch, "seq_len": f"prompts U[{lo},{hi}] + {steps} decode",
-                   "parallelism": f"tp{world}", "page_size": 16,
-                   "weights": "random N(0,0.02) bf16",
-                   "decode_allreduce": (allreduce if world > 1 else "none")},
-        "first_step_s (prefill of all + 1 decode)": round(first_s, 3),
-        "model_init_s": round(init_s, 2), "graph_capture_s": round(capture_s, 2),
-        "decode_steps_timed": n_dec, "all_requests_complete": ok, "clocks": clk,
+                               "admitted at once, greedy", "model": r["model"],
+                   "global_batch": batch, "seq_len": f"prompts {r['prompt_lens']} + {steps} decode",
+                   "parallelism": r["parallelism"], "page_size": 16, "weights": r["weights"],
+                   "decode_allreduce": r["decode_allreduce"]},
+        "first_step_s (prefill of all + 1 decode)": r["first_step_s (prefill of all + 1 decode)"],
+        "model_init_s": r["model_init_s"], "graph_capture_s": r["graph_capture_s"],
+        "decode_steps_timed": r["decode_steps_timed"],
+        "all_requests_complete": r["all_requests_complete"], "clocks": r["clocks"],
     }
     print(json.dumps(line), flush=True)
 
@@ -577,15 +627,14 @@ def cpu_reference_config1(steps=8, seed=1234):
                 "mean of all but the first")
 
 
-def run_config1(args):
+def config1_measure(dev, cpu_ms=None) -> dict:
     """BASELINE config 1 on one GPU: Qwen2.5-0.5B shape, fp32, the 4 prompts,
-    50 output tokens each, CUDA-graph decode; decode step time beside the
-    reference's CPU decode step on the same workload."""
+    50 output tokens each, CUDA-graph decode; the median decode step beside
+    the reference's CPU decode step on the same workload (``cpu_ms``, timed
+    by the caller, or here when not given)."""
     import torch
     from mi_b200.model import PRESETS, Model
     from mi_b200.scheduler import Request, Scheduler
-    dev = torch.device("cuda", 0)
-    torch.cuda.set_device(dev)
     cfg = PRESETS["qwen2.5-0.5b"]
     model = Model.create(cfg, dev, torch.float32, seed=1234)
     prompts = config1_prompts(cfg.vocab_size)
@@ -602,36 +651,44 @@ def run_config1(args):
             sched.step()
             step_ms.append((time.perf_counter() - t0) * 1e3)
     gpu_ms = statistics.median(step_ms[1:])
+    sched.close()
     del sched, model
     torch.cuda.empty_cache()
-    cpu_ms, sample = cpu_reference_config1()
-    print(json.dumps({"metric": "config 1 decode step (Qwen2.5-0.5B shape, fp32, B=4)",
-                      "value": round(gpu_ms, 3), "unit": "ms", "higher_is_better": False,
-                      "n_gpus": 1, "cuda_graph_decode": True,
-                      "cpu_reference_ms": round(cpu_ms, 2), "cpu_sample": sample}),
-          flush=True)
+    sample = "timed by the caller (cpu_baseline.config1_decode_step_ms)"
+    if cpu_ms is None:
+        cpu_ms, sample = cpu_reference_config1()
+    return {"metric": "config 1 decode step (Qwen2.5-0.5B shape, fp32, B=4)",
+            "value": round(gpu_ms, 3), "unit": "ms", "higher_is_better": False,
+            "cuda_graph_decode": True, "decode_steps": len(step_ms) - 1,
+            "cpu_reference_ms": round(cpu_ms, 2), "cpu_sample": sample,
+            "speedup_vs_cpu_reference": round(cpu_ms / gpu_ms, 1)}
 
 
-def run_prefill(args):
+def run_config1(args):
+    """``--workload config1``: ``config1_measure`` on its own."""
+    import torch
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    r = config1_measure(dev)
+    print(json.dumps({**r, "n_gpus": 1}), flush=True)
+
+
+def prefill_measure(dev, layers=8, steps=5, warmup=3) -> dict:
     """Kernel 3 on its own: ragged causal paged prefill of config 3's prompts.
 
     32 requests, prompts U[128, 1024] (seeded), Mistral-7B attention shape
     (32 Q / 8 KV heads, head_dim 128), bf16, page_size 16, random
     non-contiguous page tables, K/V already in the pages (as after the append
     of the same step). One launch per layer, each layer with its own pool;
-    ``--steps`` passes over ``--layers`` pools back to back, CUDA events
-    around the whole loop. Reports tensor TFLOP/s against the measured dense
-    bf16 peak (the burst figure: the kernel is timed alone).
+    ``steps`` passes over ``layers`` pools back to back, CUDA events around
+    the whole loop. Reports tensor TFLOP/s against the measured dense bf16
+    peak (the burst figure: the kernel is timed alone).
     """
     import torch
-    from mi_b200 import capi
     from mi_b200.prefill import BatchPrefillWithPagedKVCacheWrapper
 
-    rank, world, local = dist_env()
-    dev = torch.device("cuda", local)
-    torch.cuda.set_device(dev)
     hq, hkv, d, ps = 32, 8, 128, 16
-    L = min(args.layers, 8)
+    L = min(layers, 8)
     rng = np.random.default_rng(3)
     lens = rng.integers(128, 1025, 32).tolist()
     npages = [math.ceil(n / ps) for n in lens]
@@ -654,13 +711,13 @@ def run_prefill(args):
     ws = torch.zeros(64 << 20, dtype=torch.uint8, device=dev)
     w = BatchPrefillWithPagedKVCacheWrapper(ws)
     w.plan(qo_t, ip, ind, lp, hq, hkv, d, ps, causal=True, q_data_type=torch.bfloat16)
-    for i in range(max(args.warmup, 3)):
+    for i in range(max(warmup, 3)):
         for pool in pools:
             w.run(q, pool, out=out)
     torch.cuda.synchronize()
     w.check_status()
-    K = max(1, min(args.steps, 20))
-    clocks = ClockSampler(local)
+    K = max(1, min(steps, 20))
+    clocks = ClockSampler(dev.index or 0)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for _ in range(K):
@@ -673,25 +730,40 @@ def run_prefill(args):
     ms = e0.elapsed_time(e1) / (K * L)
     fl = prefill_flops(lens, hq, d)
     tflops = fl / (ms / 1e3) / 1e12
-    peak = None
     try:
         with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as f:
             peak = float(json.load(f)["bf16_tflops"])
         kind = "measured"
-    except (OSError, KeyError, ValueError):
+    except (OSError, KeyError, TypeError, ValueError):  # absent or malformed: the fallback
         peak, kind = 1590.0, "fallback"
-    line = {"metric": "paged prefill attention TFLOP/s (config-3 prompts)",
-            "value": round(tflops, 1), "unit": "TFLOP/s", "n_gpus": 1, "steps": K,
-            "warmup": max(args.warmup, 3), "ms_per_step": round(ms, 4),
-            "higher_is_better": True, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": "ragged causal paged prefill, 32 requests, prompts "
-                                   "U[128,1024] seeded, 32 Q / 8 KV heads, head_dim 128, "
-                                   "page_size 16", "tokens": qo[-1], "layers_pools": L},
+    del pools
+    torch.cuda.empty_cache()
+    return {"metric": "paged prefill attention TFLOP/s (config-3 prompts)",
+            "value": round(tflops, 1), "unit": "TFLOP/s", "steps": K,
+            "warmup": max(warmup, 3), "ms_per_launch": round(ms, 4),
+            "workload": ("ragged causal paged prefill, 32 requests, prompts U[128,1024] seeded, "
+                         "32 Q / 8 KV heads, head_dim 128, page_size 16"),
+            "tokens": qo[-1], "layers_pools": L,
             "roofline": {"bound": "tensor", "kernel": "prefill_tc_kernel",
                          "achieved": round(tflops, 1), "peak": peak, "unit": "TFLOP/s",
-                         "frac": round(tflops / peak, 4), "peak_kind": kind,
+                         "frac": round(tflops / peak, 4), "peak_kind": f"{kind} (burst)",
                          "algorithmic_flops": fl, "avg_launch_us": round(ms * 1e3, 2)},
             "clocks": clk, "gpu_launches": K * L}
+
+
+def run_prefill(args):
+    """``--workload prefill``: ``prefill_measure`` on its own."""
+    import torch
+    rank, world, local = dist_env()
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    r = prefill_measure(dev, layers=args.layers, steps=args.steps, warmup=args.warmup)
+    line = {"metric": r["metric"], "value": r["value"], "unit": "TFLOP/s", "n_gpus": 1,
+            "steps": r["steps"], "warmup": r["warmup"], "ms_per_step": r["ms_per_launch"],
+            "higher_is_better": True, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": r["workload"], "tokens": r["tokens"],
+                       "layers_pools": r["layers_pools"]},
+            "roofline": r["roofline"], "clocks": r["clocks"], "gpu_launches": r["gpu_launches"]}
     print(json.dumps(line), flush=True)
 
 
@@ -706,9 +778,18 @@ def parse_args():
                     help="layer pools per step (32 = Mistral-7B; fewer only for profiling)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--shard", choices=["replicas", "heads"], default="replicas",
-                    help="config 2 on N GPUs: N replicas (weak scaling) or the KV heads "
-                         "split over the GPUs (strong scaling)")
+    ap.add_argument("--shard", choices=["auto", "replicas", "heads"], default="auto",
+                    help="config 2 on N GPUs: the KV heads split over the GPUs (strong "
+                         "scaling; the default for N > 1, with the replicas split reported "
+                         "beside it) or N replicas (weak scaling)")
+    ap.add_argument("--no-tp", action="store_true",
+                    help="N > 1: skip the Qwen2.5-72B tensor-parallel decode (config 5)")
+    ap.add_argument("--tp-steps", type=int, default=48,
+                    help="N > 1: decode steps of the config-5 measurement")
+    ap.add_argument("--no-extra", action="store_true",
+                    help="N = 1: skip the prefill, churn (config 4) and config-1 measurements")
+    ap.add_argument("--churn-requests", type=int, default=96,
+                    help="N = 1: requests served in the churn (config 4) measurement")
     ap.add_argument("--no-model", action="store_true",
                     help="skip the Mistral-7B-shape decode measurement (config 3)")
     ap.add_argument("--workload",
@@ -776,42 +857,19 @@ def workload_config(shard="replicas", world=1):
                   "(~285 MB of KV per layer)"}
 
 
-def main():
-    args = parse_args()
-    if args.impl == "reference":
-        run_reference(args)
-        return
-    if args.workload == "config5":
-        run_tp_decode(args)
-        return
-    if args.workload == "config4":
-        run_churn(args)
-        return
-    if args.workload == "prefill":
-        run_prefill(args)
-        return
-    if args.workload == "decode-shapes":
-        run_decode_shapes(args)
-        return
-    if args.workload == "config1":
-        run_config1(args)
-        return
+def run_config2(args, rank, world, local, dev, heads: bool, with_e2e: bool = True) -> dict:
+    """BASELINE config 2 on this rank: the timed steps, the roofline loops and
+    (optionally) the end-to-end graph. Returns the measured numbers; the
+    caller assembles the JSON line. ``heads``: this rank holds KV heads
+    [rank * 8/N, (rank+1) * 8/N) of every page (and their query heads)."""
     import torch
     import torch.distributed as dist
-    from datetime import timedelta
 
     from mi_b200.decode import BatchDecodeWithPagedKVCacheWrapper
     from mi_b200.rope import rope_tables
 
-    rank, world, local = dist_env()
-    if world > 1:
-        dist.init_process_group("nccl", timeout=timedelta(seconds=120),
-                                device_id=torch.device("cuda", local))
-    dev = torch.device("cuda", local)
-    torch.cuda.set_device(dev)
-    CFG["layers"] = args.layers
     c = dict(CFG)
-    heads = args.shard == "heads" and world > 1
+    c["layers"] = args.layers
     if heads:
         # head-sharded config 2: rank r decodes KV heads [r * hkv/N, (r+1) * hkv/N)
         # (and their query heads) of every request; no exchange between ranks
@@ -978,7 +1036,7 @@ def main():
     # drains each layer's output as soon as its decode is done. The eager form
     # (same calls issued one by one on one stream) is reported beside it.
     e2e = None
-    if not args.no_e2e:
+    if with_e2e:
         nq, nk = b * hq * d, b * hkv * d
         seg = nq + 2 * nk
         in_h = torch.randn(L, seg, dtype=torch.bfloat16).pin_memory()
@@ -1064,54 +1122,127 @@ def main():
                "eager": {"value": gbs(eager_ms), "ms_per_step": round(eager_ms, 4),
                          "timing": "same calls issued one by one on one stream"}}
 
-    # ---- CPU baseline (rank 0, N = 1 only) ------------------------------------
-    cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        gbs, _, threads, sample = cpu_reference_steps(lens, 8, budget_s=20.0)
-        cpu = {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
-               "sample": sample}
-        # the same path in fp32 (the reference's CPU dtype for config 1)
-        gbs32, _, _, sample32 = cpu_reference_steps(lens, 4, budget_s=10.0,
-                                                    dtype_name="float32")
-        cpu["fp32"] = {"value": round(gbs32, 3), "unit": "GB/s", "sample": sample32}
-        # the reference's whole CPU decode step at config 1 (its own workload)
-        c1_ms, c1_sample = cpu_reference_config1()
-        cpu["config1_decode_step_ms"] = {"value": round(c1_ms, 2), "unit": "ms",
-                                         "sample": c1_sample}
+    return {"value": value, "ms_per_step": ms_per_step, "K": K, "L": L,
+            "peak": peak, "peak_kind": peak_kind, "achieved": achieved, "traffic": traffic,
+            "algorithmic_bytes": decode_bytes(lens, c) + append_bytes(b, c),
+            "dec_ms": dec_ms, "two_call_ms": two_call_ms, "kd": kd, "clocks": clk, "e2e": e2e}
 
-    # ---- config 3: model decode tok/s (rank 0, N = 1) --------------------------
-    model_line = None
-    if rank == 0 and world == 1 and not args.no_model:
-        del pools
+
+def cpu_baseline_line(lens) -> dict:
+    """The reference's own CPU path on this host (rank 0, N = 1)."""
+    gbs, _, threads, sample = cpu_reference_steps(lens, 8, budget_s=20.0)
+    cpu = {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+           "sample": sample}
+    # the same path in fp32 (the reference's CPU dtype for config 1)
+    gbs32, _, _, sample32 = cpu_reference_steps(lens, 4, budget_s=10.0, dtype_name="float32")
+    cpu["fp32"] = {"value": round(gbs32, 3), "unit": "GB/s", "sample": sample32}
+    # the reference's whole CPU decode step at config 1 (its own workload)
+    c1_ms, c1_sample = cpu_reference_config1()
+    cpu["config1_decode_step_ms"] = {"value": round(c1_ms, 2), "unit": "ms", "sample": c1_sample}
+    return cpu
+
+
+def roofline_obj(r: dict, heads: bool) -> dict:
+    return {"bound": "hbm", "kernel": "decode_sk_kernel (append fused in)",
+            "achieved": round(r["achieved"], 1), "peak": r["peak"], "unit": "GB/s",
+            "frac": round(r["achieved"] / r["peak"], 4), "peak_kind": r["peak_kind"],
+            "traffic": r["traffic"] if not heads else None,
+            "algorithmic_bytes": r["algorithmic_bytes"],
+            "avg_launch_us": round(r["dec_ms"] * 1e3, 2),
+            "two_call_us": round(r["two_call_ms"] * 1e3, 2),
+            "timing": (f"CUDA events around {r['kd'] * r['L']} back-to-back launch pairs "
+                       "(fused append + decode, split-K merge) over the layer pools; "
+                       "two_call_us: the same layers as the append kernel followed by "
+                       "the plain decode pair, timed right after"),
+            "gpu_launches_roofline_loop": 2 * r["kd"] * r["L"]}
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+        return
+    if args.workload == "config5":
+        run_tp_decode(args)
+        return
+    if args.workload == "config4":
+        run_churn(args)
+        return
+    if args.workload == "prefill":
+        run_prefill(args)
+        return
+    if args.workload == "decode-shapes":
+        run_decode_shapes(args)
+        return
+    if args.workload == "config1":
+        run_config1(args)
+        return
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    rank, world, local = dist_env()
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=dev)
+    heads = world > 1 and args.shard != "replicas"
+    if heads and CFG["hkv"] % world:
+        raise SystemExit(f"head sharding needs {CFG['hkv']} KV heads divisible by {world}")
+    lens = config2_lens(CFG["seed"])
+    r = run_config2(args, rank, world, local, dev, heads, with_e2e=not args.no_e2e)
+
+    # ---- N > 1: the other split of config 2, and the tensor-parallel model ----
+    replicas = tp = None
+    if world > 1 and heads:
         torch.cuda.empty_cache()
-        model_line = model_decode(dev)
+        rr = run_config2(args, rank, world, local, dev, False, with_e2e=False)
+        replicas = {"value": round(rr["value"], 2), "unit": "GB/s",
+                    "ms_per_step": round(rr["ms_per_step"], 4), "scaling": "weak",
+                    "parallelism": "replicas: every GPU runs the whole config-2 step on its own "
+                                   "pools (no collective)",
+                    "roofline": roofline_obj(rr, False), "clocks": rr["clocks"]}
+        torch.cuda.empty_cache()
+    if world > 1 and not args.no_tp:
+        tp = tp_decode(args, rank, world, local, dev, batch=64, steps=args.tp_steps)
+        torch.cuda.empty_cache()
+
+    # ---- N = 1: CPU baseline and the other single-GPU workloads (rank 0) -------
+    cpu = model_line = prefill = churn = c1 = None
+    if rank == 0 and world == 1:
+        if not args.no_cpu_baseline:
+            cpu = cpu_baseline_line(lens)
+        torch.cuda.empty_cache()
+        if not args.no_model:
+            model_line = model_decode(dev)
+        if not args.no_extra:
+            prefill = prefill_measure(dev, layers=8, steps=5, warmup=3)
+            churn = churn_measure(dev, n_req=args.churn_requests)
+            c1 = config1_measure(dev, cpu_ms=(cpu or {}).get("config1_decode_step_ms",
+                                                             {}).get("value"))
 
     if world > 1:
         dist.destroy_process_group()
     if rank != 0:
         return
     line = {
-        "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
-        "steps": K, "warmup": max(args.warmup, 3), "ms_per_step": round(ms_per_step, 4),
+        "metric": METRIC, "value": round(r["value"], 2), "unit": "GB/s", "n_gpus": world,
+        "steps": r["K"], "warmup": max(args.warmup, 3), "ms_per_step": round(r["ms_per_step"], 4),
         "higher_is_better": True, "scaling": "strong" if heads else "weak",
         "vs_baseline": None, "dtype": "bf16",
-        "data": "synthetic", "config": workload_config(args.shard, world),
-        "roofline": {"bound": "hbm", "kernel": "decode_sk_kernel (append fused in)",
-                     "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                     "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
-                     "traffic": traffic if not heads else None,
-                     "algorithmic_bytes": decode_bytes(lens, c) + append_bytes(b, c),
-                     "avg_launch_us": round(dec_ms * 1e3, 2),
-                     "two_call_us": round(two_call_ms * 1e3, 2),
-                     "timing": (f"CUDA events around {kd * L} back-to-back launch pairs "
-                                "(fused append + decode, split-K merge) over the layer pools; "
-                                "two_call_us: the same layers as the append kernel followed by "
-                                "the plain decode pair, timed right after"),
-                     "gpu_launches_roofline_loop": 2 * kd * L},
-        "cpu_baseline": cpu, "e2e": e2e, "clocks": clk,
-        "gpu_launches": 2 * K * L,
+        "data": "synthetic", "config": workload_config("heads" if heads else "replicas", world),
+        "roofline": roofline_obj(r, heads),
+        "cpu_baseline": cpu, "e2e": r["e2e"], "clocks": r["clocks"],
+        "gpu_launches": 2 * r["K"] * r["L"],
         "model_decode": model_line,
     }
+    if replicas is not None:
+        line["replicas"] = replicas
+    if tp is not None:
+        line["tp_decode"] = tp
+    for key, val in (("prefill", prefill), ("churn", churn), ("config1", c1)):
+        if val is not None:
+            line[key] = val
     print(json.dumps(line), flush=True)
 
 
