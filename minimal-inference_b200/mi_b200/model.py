@@ -40,6 +40,7 @@ import torch.nn.functional as F
 
 from .glue import add_rmsnorm, silu_mul
 from .page import append_paged_kv_cache
+from .weights import load_weights  # noqa: F401  (server.py imports it from the model module)
 from .rope import rope_tables
 
 

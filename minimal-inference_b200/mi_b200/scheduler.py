@@ -233,6 +233,13 @@ class Scheduler:
         device = torch.device(device)
         if device.type != "cuda":
             raise RuntimeError("mi_b200.Scheduler runs on a CUDA device (no CPU fallback)")
+        # a model built the way server.py builds it (Model(cfg), load_weights,
+        # .to(...).eval()) still has trainable parameters and unfused GEMM
+        # weights: this is an inference engine, and the graphs below must
+        # capture the fused weights
+        model.requires_grad_(False)
+        if getattr(model.layers[0].self_attn, "_qkv_wt", None) is None:
+            model.prepare()
         self.model, self.config = model, config
         self.device, self.dtype = device, dtype
         self.max_batch_size, self.max_seq_len, self.page_size = max_batch_size, max_seq_len, page_size

@@ -77,6 +77,8 @@ def load_weights(model: torch.nn.Module, model_path: str, device="cpu",
     missing, unexpected = model.load_state_dict(cleaned, strict=False)
     real_missing = [k for k in missing if "cached" not in k]
     if real_missing:
-        print(f"Warning: missing keys: {real_missing}")
+        print(f"load_weights: {len(real_missing)} model parameters absent from the "
+              f"checkpoint (left as they were): {real_missing}")
     if unexpected:
-        print(f"Warning: unexpected keys: {unexpected}")
+        print(f"load_weights: {len(unexpected)} checkpoint tensors with no model parameter "
+              f"(ignored): {unexpected}")
