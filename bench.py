@@ -767,6 +767,89 @@ def run_prefill(args):
     print(json.dumps(line), flush=True)
 
 
+def run_flashinfer_context(args):
+    """Context, not a baseline arm: the reference's own GPU path for one
+    config-2 layer on this GPU -- stock ``flashinfer.page.append_paged_kv_cache``
+    plus ``BatchDecodeWithPagedKVCacheWrapper`` constructed and planned as the
+    reference does (scheduler.py:535-539, :905-916; model.py:207-216, :235) --
+    over the same pools, page tables and contexts as ``run_config2`` (8 layer
+    pools, ~5 GB, so every launch reads from HBM). The reference's RoPE
+    (torch elementwise ops) and per-step ``plan()`` are not counted."""
+    import torch
+    try:
+        import flashinfer
+    except ImportError as e:
+        print(json.dumps({"workload": "flashinfer-context", "unavailable": str(e)}), flush=True)
+        return
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    c = CFG
+    b, hq, hkv, d, ps, P, L = (c["batch"], c["hq"], c["hkv"], c["head_dim"], c["page_size"],
+                               c["num_pages"], 8)
+    lens = config2_lens(c["seed"], b, c["ctx_lo"], c["ctx_hi"])
+    perm = np.random.default_rng(c["seed"]).permutation(P - 1)
+    indptr, indices, last, k0 = [0], [], [], 0
+    for n in lens:
+        k = math.ceil(n / ps)
+        indices.extend(perm[k0:k0 + k].tolist())
+        k0 += k
+        indptr.append(len(indices))
+        last.append(n % ps or ps)
+    i32 = lambda x: torch.tensor(x, dtype=torch.int32, device=dev)  # noqa: E731
+    ip, ind, lp = i32(indptr), i32(indices), i32(last)
+    g = torch.Generator(device=dev).manual_seed(1234)
+    pools = [torch.randn(P, 2, ps, hkv, d, device=dev, dtype=torch.bfloat16, generator=g)
+             for _ in range(L)]
+    q = torch.randn(b, hq, d, device=dev, dtype=torch.bfloat16, generator=g)
+    kn = torch.randn(b, hkv, d, device=dev, dtype=torch.bfloat16, generator=g)
+    vn = torch.randn(b, hkv, d, device=dev, dtype=torch.bfloat16, generator=g)
+    bi = torch.arange(b, dtype=torch.int32, device=dev)
+    pos = i32([n - 1 for n in lens])
+    t0 = time.perf_counter()
+    ws = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    w = flashinfer.decode.BatchDecodeWithPagedKVCacheWrapper(ws, kv_layout="NHD")
+    w.plan(indptr=ip, indices=ind, last_page_len=lp, num_qo_heads=hq, num_kv_heads=hkv,
+           head_dim=d, page_size=ps, pos_encoding_mode="NONE", q_data_type=torch.bfloat16,
+           data_type=torch.bfloat16)
+
+    def layer(pool):
+        flashinfer.page.append_paged_kv_cache(kn, vn, bi, pos, pool, ind, ip, lp, kv_layout="NHD")
+        return w.run(q, pool)
+
+    for _ in range(max(args.warmup, 3)):
+        for pool in pools:
+            layer(pool)
+    torch.cuda.synchronize()
+    setup_s = time.perf_counter() - t0
+
+    def timed(fn, reps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            for pool in pools:
+                fn(pool)
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) * 1e3 / (reps * L)
+
+    reps = max(1, min(args.steps, 20))
+    clocks = ClockSampler(0)
+    us_pair = timed(layer, reps)
+    us_dec = timed(lambda pool: w.run(q, pool), reps)
+    clk = clocks.stop()
+    peak, kind = read_peak()
+    byt = decode_bytes(lens)
+    print(json.dumps({
+        "workload": "flashinfer-context", "metric": "reference GPU path (FlashInfer) at config 2",
+        "flashinfer": flashinfer.__version__, "append_plus_decode_us": round(us_pair, 2),
+        "decode_us": round(us_dec, 2), "decode_gbs": round(byt / us_dec / 1e3, 1),
+        "decode_frac": round(byt / us_dec / 1e3 / peak, 4), "peak_kind": kind,
+        "setup_s (JIT / module load, plan, warm-up)": round(setup_s, 1), "layer_pools": L,
+        "reps": reps, "clocks": clk,
+        "note": "context only; the reference's RoPE ops and per-step plan() are not counted"}),
+        flush=True)
+
+
 # ---------------------------------------------------------------------------
 def parse_args():
     ap = argparse.ArgumentParser()
@@ -794,7 +877,7 @@ def parse_args():
                     help="skip the Mistral-7B-shape decode measurement (config 3)")
     ap.add_argument("--workload",
                     choices=["config2", "config1", "config4", "config5", "prefill",
-                             "decode-shapes"],
+                             "decode-shapes", "flashinfer-context"],
                     default="config2",
                     help="config5: Qwen2.5-72B tensor-parallel decode over the launch's GPUs; "
                          "prefill: the paged prefill kernel alone on config 3's prompts")
@@ -1176,6 +1259,9 @@ def main():
         return
     if args.workload == "config1":
         run_config1(args)
+        return
+    if args.workload == "flashinfer-context":
+        run_flashinfer_context(args)
         return
     import torch
     import torch.distributed as dist
