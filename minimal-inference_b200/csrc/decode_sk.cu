@@ -60,11 +60,14 @@ constexpr size_t kCtrl = 256;
 // Stream-K split: what a request start inside a run costs its CTA, in bytes
 // of page stream. A segment boundary stalls the CTA's consumers for ~3.5 us
 // (the previous segment's combine, the next one's query loads), about 154 KB
-// of one SM's share of HBM bandwidth; but a run shortened by k pages does
-// not finish k pages' time sooner, and on config 2 (B200, 8 KV heads) a
-// sweep of 154 / 300 / 450 / 650 KB gave 52.6 / 51.3 / 51.3 / 51.7 us per
-// launch pair.
-constexpr double kSegCostBytes = 380e3;
+// of one SM's share of HBM bandwidth. Measured on a B200: with 8 KV heads a
+// run shortened by k pages does not finish k pages' time sooner, and config
+// 2's fused step (B=32) took 52.6 / 51.3 / 51.3 / 51.7 us per launch pair at
+// 154 / 300 / 450 / 650 KB; with 1-4 KV heads (tensor-parallel and
+// head-sharded shapes, B=32 and 64) 154 KB stayed within 3.3 % of the best
+// of 0 / 60 / 154 / 380 KB on every shape, and 380 KB lost up to 13 %.
+constexpr double kSegCostBytesWide = 380e3;  // 8 or more KV heads
+constexpr double kSegCostBytes = 154e3;      // fewer
 
 inline size_t al256(size_t x) { return (x + 255) & ~size_t(255); }
 
@@ -1022,7 +1025,7 @@ int launch_decode_sk(const SkArgs &a) {
   p.rope_off = L.rope_off;
   {
     const double page_bytes = double(a.ps) * a.hkv * a.d * 2 * 2;
-    const double c = 4.0 * kSegCostBytes / page_bytes;
+    const double c = 4.0 * (a.hkv >= 8 ? kSegCostBytesWide : kSegCostBytes) / page_bytes;
     p.seg_cost4 = static_cast<int>(c > 4096.0 ? 4096.0 : c + 0.5);
   }
   if (a.k_new != nullptr) {
