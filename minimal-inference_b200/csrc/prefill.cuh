@@ -27,5 +27,8 @@ struct PrefillParams {
 // shape or layout is outside its coverage, so the caller runs the generic
 // kernel instead.
 int launch_prefill_tc(const PrefillParams &p, int dtype, cudaStream_t s);
+// Two query tiles per work item (prefill_tc2.cu), the same coverage; -1 when
+// outside it.
+int launch_prefill_tc2(const PrefillParams &p, int dtype, cudaStream_t s);
 
 }  // namespace mi
