@@ -744,7 +744,7 @@ def prefill_measure(dev, layers=8, steps=5, warmup=3) -> dict:
             "workload": ("ragged causal paged prefill, 32 requests, prompts U[128,1024] seeded, "
                          "32 Q / 8 KV heads, head_dim 128, page_size 16"),
             "tokens": qo[-1], "layers_pools": L,
-            "roofline": {"bound": "tensor", "kernel": "prefill_tc_kernel",
+            "roofline": {"bound": "tensor", "kernel": "prefill_tc2_kernel",
                          "achieved": round(tflops, 1), "peak": peak, "unit": "TFLOP/s",
                          "frac": round(tflops / peak, 4), "peak_kind": f"{kind} (burst)",
                          "algorithmic_flops": fl, "avg_launch_us": round(ms * 1e3, 2)},

@@ -141,7 +141,10 @@ extern "C" int mi_paged_prefill(
   if (workspace && workspace_bytes >= 256 && (reinterpret_cast<uintptr_t>(workspace) & 15) == 0)
     p.ctr = static_cast<unsigned *>(workspace);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  const int rc = launch_prefill_tc(p, dtype, s);
+  // tensor cores: two query tiles per work item, else one
+  int rc = launch_prefill_tc2(p, dtype, s);
+  if (rc >= 0) return rc;
+  rc = launch_prefill_tc(p, dtype, s);
   if (rc >= 0) return rc;
   switch (dtype) {
     case MI_DTYPE_F32: return launch_generic<float>(p, s);
