@@ -466,17 +466,17 @@ __global__ void __launch_bounds__(kThreads2, 1)
         // pass 1: the row max over the tile's keys (raw scores; the scale is
         // folded into the exponent's FMA)
         float mt = -INFINITY;
-#pragma unroll 2
-        for (int c = 0; c < kN / 16; ++c) {
-          float sv[16];
-          tmem_ld16(tmem_s + c * 16, sv);
+#pragma unroll 1
+        for (int c = 0; c < kN / 32; ++c) {
+          float sv[32];
+          tmem_ld32(tmem_s + c * 32, sv);
           tmem_wait_ld();
           if (masked) {
 #pragma unroll
-            for (int i = 0; i < 16; ++i) sv[i] = (kbase + c * 16 + i < lim) ? sv[i] : -INFINITY;
+            for (int i = 0; i < 32; ++i) sv[i] = (kbase + c * 32 + i < lim) ? sv[i] : -INFINITY;
           }
 #pragma unroll
-          for (int i = 0; i < 16; ++i) mt = fmaxf(mt, sv[i]);
+          for (int i = 0; i < 32; ++i) mt = fmaxf(mt, sv[i]);
         }
         mt *= p.scale_log2;  // scale_log2 > 0: the max commutes with it
         // keep the old max unless this tile's exceeds it by > kRescaleLog2
@@ -484,24 +484,24 @@ __global__ void __launch_bounds__(kThreads2, 1)
         const float ms = m_new == -INFINITY ? 0.f : m_new;
         const float corr = m == m_new ? 1.f : fast_exp2(m - ms);
         // pass 2: P = 2^(s * scale - m) as 16-bit pairs over the S columns
-        // already read (chunk c's P lands in columns [8 c, 8 c + 8))
+        // already read (chunk c's P lands in columns [16 c, 16 c + 16))
         float sum = 0.f;
-#pragma unroll 2
-        for (int c = 0; c < kN / 16; ++c) {
-          float sv[16];
-          tmem_ld16(tmem_s + c * 16, sv);
+#pragma unroll 1
+        for (int c = 0; c < kN / 32; ++c) {
+          float sv[32];
+          tmem_ld32(tmem_s + c * 32, sv);
           tmem_wait_ld();
-          uint32_t pk[8];
+          uint32_t pk[16];
 #pragma unroll
-          for (int i = 0; i < 16; i += 2) {
-            const bool in0 = !masked || kbase + c * 16 + i < lim;
-            const bool in1 = !masked || kbase + c * 16 + i + 1 < lim;
+          for (int i = 0; i < 32; i += 2) {
+            const bool in0 = !masked || kbase + c * 32 + i < lim;
+            const bool in1 = !masked || kbase + c * 32 + i + 1 < lim;
             const float p0 = in0 ? fast_exp2(fmaf(sv[i], p.scale_log2, -ms)) : 0.f;
             const float p1 = in1 ? fast_exp2(fmaf(sv[i + 1], p.scale_log2, -ms)) : 0.f;
             sum += p0 + p1;
             pk[i >> 1] = Pack2<T>::run(p0, p1);
           }
-          tmem_st8(tmem_s + c * 8, pk);
+          tmem_st16(tmem_s + c * 16, pk);
         }
         l = l * corr + sum;
         m = m_new;

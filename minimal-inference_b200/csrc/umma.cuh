@@ -138,15 +138,6 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float *v) {
   for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-// 8 consecutive 32-bit TMEM columns of this thread's lane.
-__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t *v) {
-  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(
-                   taddr),
-               "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]),
-               "r"(v[7])
-               : "memory");
-}
-
 // 16 consecutive 32-bit TMEM columns of this thread's lane.
 __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t *v) {
   asm volatile(
