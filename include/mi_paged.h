@@ -313,6 +313,18 @@ int mi_add_rmsnorm(const void *x, void *residual, const void *weight, void *out,
 int mi_silu_mul(const void *gate_up, void *out, int32_t rows, int32_t inter, int32_t dtype,
                 mi_stream_t stream);
 
+/* y[r, :] = x[r, :] w^T (+ bias) for m <= 32 rows: the reference's
+ * nn.Linear projections (model.py:127-131, :306-308) at decode batch sizes,
+ * where the weight is streamed once from HBM. x [m, k] (row stride ldx),
+ * w [n, k] (row stride ldw; the nn.Linear layout), y [m, n] (row stride
+ * ldy), bias [n] or NULL; bf16 / fp16 with fp32 accumulation, one rounding
+ * at the end; k a multiple of 64; pointers 16-byte aligned, ldx / ldw
+ * multiples of 8. Deterministic: K-split partial sums are added in a fixed
+ * order. No workspace; m = 0 launches nothing. */
+int mi_proj_small_m(const void *x, int64_t ldx, const void *w, int64_t ldw, const void *bias,
+                    void *y, int64_t ldy, int32_t m, int32_t n, int32_t k, int32_t dtype,
+                    int32_t *status, mi_stream_t stream);
+
 /* ---- tensor parallelism: fused all-reduce for decode steps --------------- */
 
 /* No FlashInfer counterpart: replaces, for decode-sized row counts, the

@@ -81,6 +81,8 @@ _SIGS = {
                         ctypes.c_int),
     "mi_add_rmsnorm": ([_c_p, _c_p, _c_p, _c_p, _c_i32, _c_i32, _c_f, _c_i32, _c_p], ctypes.c_int),
     "mi_silu_mul": ([_c_p, _c_p, _c_i32, _c_i32, _c_i32, _c_p], ctypes.c_int),
+    "mi_proj_small_m": ([_c_p, _c_i64, _c_p, _c_i64, _c_p, _c_p, _c_i64, _c_i32, _c_i32, _c_i32,
+                         _c_i32, _c_p, _c_p], ctypes.c_int),
     "mi_allreduce_add_rmsnorm": ([_c_p, _c_i64, _c_i64, _c_p, _c_i32, _c_i32, _c_p, _c_p, _c_p,
                                  _c_i32, _c_i32, _c_f, _c_i32, _c_p, _c_p], ctypes.c_int),
     "mi_set_peer_wait_limit_ns": ([_c_i64], ctypes.c_int),

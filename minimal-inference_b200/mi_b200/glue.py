@@ -59,3 +59,59 @@ def silu_mul(gate_up: torch.Tensor, out: torch.Tensor | None = None) -> torch.Te
     capi.call("mi_silu_mul", ptr(gate_up), ptr(out), rows, inter, dtype_code(gate_up.dtype),
               stream_of(gate_up))
     return out
+
+
+_PROJ_STATUS: dict[int, torch.Tensor] = {}
+PROJ_MAX_ROWS = 32
+
+
+def proj_status(device: torch.device) -> torch.Tensor:
+    """The int32 status word proj_small_m calls on ``device`` OR their
+    MI_STATUS_* bits into (MI_STATUS_TIMEOUT: a bounded wait gave up)."""
+    idx = device.index or 0
+    st = _PROJ_STATUS.get(idx)
+    if st is None:
+        st = _PROJ_STATUS[idx] = torch.zeros(1, dtype=torch.int32, device=device)
+    return st
+
+
+def proj_small_m(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = None,
+                 out: torch.Tensor | None = None,
+                 status: torch.Tensor | None = None) -> torch.Tensor:
+    """``x @ weight.T (+ bias)`` for ``x`` of at most 32 rows: ``F.linear``
+    at decode batch sizes, streaming ``weight`` ([n, k], the nn.Linear
+    layout, rows contiguous) once from HBM (``mi_proj_small_m``).
+
+    ``x`` is ``[..., k]`` with contiguous rows (row stride >= k), ``out`` (if
+    given) ``[..., n]`` with contiguous rows; one dtype (bf16 / fp16)
+    throughout; ``k`` a multiple of 64. ``status``: int32 device word for
+    MI_STATUS_* bits (default: ``proj_status(device)``)."""
+    k = x.shape[-1]
+    n = weight.shape[0]
+    x2 = x.reshape(-1, k)
+    m = x2.shape[0]
+    if m > PROJ_MAX_ROWS:
+        raise ValueError(f"proj_small_m: {m} rows > {PROJ_MAX_ROWS}")
+    if weight.dim() != 2 or weight.shape[1] != k or weight.stride(1) != 1:
+        raise ValueError("proj_small_m: weight must be [n, k] with contiguous rows")
+    if x2.stride(-1) != 1 or weight.dtype != x.dtype:
+        raise ValueError("proj_small_m: x rows must be contiguous, of weight's dtype")
+    if bias is not None and (bias.shape != (n,) or bias.dtype != x.dtype or bias.stride(0) != 1):
+        raise ValueError("proj_small_m: bias must be a contiguous [n] of x's dtype")
+    dev = x.device
+    need_on("weight", weight, dev)
+    if out is None:
+        out = torch.empty(*x.shape[:-1], n, dtype=x.dtype, device=dev)
+    elif out.shape != (*x.shape[:-1], n) or out.dtype != x.dtype:
+        raise ValueError("proj_small_m: out must be [..., n] of x's dtype")
+    y2 = out.view(-1, n)
+    if y2.stride(-1) != 1:
+        raise ValueError("proj_small_m: out rows must be contiguous")
+    need_on("out", out, dev)
+    if m == 0:
+        return out
+    capi.call("mi_proj_small_m", ptr(x2), x2.stride(0) if m > 1 else k, ptr(weight),
+              weight.stride(0), ptr(bias), ptr(y2), y2.stride(0) if m > 1 else n, m, n, k,
+              dtype_code(x.dtype), ptr(status if status is not None else proj_status(dev)),
+              stream_of(x))
+    return out

@@ -38,7 +38,7 @@ import torch.distributed as dist
 import torch.nn as nn
 import torch.nn.functional as F
 
-from .glue import add_rmsnorm, silu_mul
+from .glue import PROJ_MAX_ROWS, add_rmsnorm, proj_small_m, silu_mul
 from .page import append_paged_kv_cache
 from .weights import load_weights  # noqa: F401  (server.py imports it from the model module)
 from .rope import rope_tables
@@ -208,6 +208,17 @@ class Attention(nn.Module):
         return torch.mm(out.view(n, hq * d), self._o_wt).view(bsz, seq_len, -1)
 
 
+def _streams_weight(x2: torch.Tensor, w: torch.Tensor) -> bool:
+    """Whether ``x2 @ w.T`` runs on the small-M projection kernel
+    (``glue.proj_small_m``): decode-sized rows, 16-bit types, K a multiple
+    of 64, aligned rows."""
+    return (x2.shape[0] <= PROJ_MAX_ROWS and x2.is_cuda and w.dtype == x2.dtype
+            and x2.dtype in (torch.bfloat16, torch.float16) and w.shape[1] % 64 == 0
+            and w.stride(1) == 1 and w.stride(0) % 8 == 0 and x2.stride(-1) == 1
+            and (x2.shape[0] <= 1 or x2.stride(0) % 8 == 0)
+            and x2.data_ptr() % 16 == 0 and w.data_ptr() % 16 == 0)
+
+
 class MLP(nn.Module):
     """SwiGLU (model.py:301-311); gate and up run as one GEMM."""
 
@@ -225,13 +236,21 @@ class MLP(nn.Module):
         with torch.no_grad():
             self._gu_wt = _fuse_rows_t([self.gate_proj.weight, self.up_proj.weight])
 
-    def forward(self, x: torch.Tensor, *, proj_out: torch.Tensor | None = None) -> torch.Tensor:
+    def forward(self, x: torch.Tensor, *, proj_out: torch.Tensor | None = None,
+                status: torch.Tensor | None = None) -> torch.Tensor:
+        """``proj_out`` (extension): ``[tokens, hidden]`` buffer down_proj
+        writes into; ``status``: device status word of the small-M kernel."""
         if self._gu_wt is None:
             self.fuse()
         act = silu_mul(torch.mm(x.reshape(-1, x.shape[-1]), self._gu_wt)).view(
             *x.shape[:-1], -1)
+        a2 = act.view(-1, act.shape[-1])
+        w = self.down_proj.weight
+        if _streams_weight(a2, w):  # decode: the weight streamed once (mi_proj_small_m)
+            y = proj_small_m(a2, w, out=proj_out, status=status)
+            return y.view(*act.shape[:-1], -1)
         if proj_out is not None:  # down_proj straight into a peer all-reduce region
-            torch.mm(act.view(-1, act.shape[-1]), self.down_proj.weight.t(), out=proj_out)
+            torch.mm(a2, w.t(), out=proj_out)
             return proj_out.view(*act.shape[:-1], -1)
         return self.down_proj(act)
 
@@ -276,7 +295,8 @@ class DecoderLayer(nn.Module):
                            proj_out=self.comm.site(site_a, rows) if peer else None)
         y = add_norm(self.comm, (a, site_a) if peer else (self._reduce(a), None), h,
                      self.post_attention_layernorm)
-        m = self.mlp(y, proj_out=self.comm.site(site_m, rows) if peer else None)
+        m = self.mlp(y, proj_out=self.comm.site(site_m, rows) if peer else None,
+                     status=getattr(attn_backend, "status", None))
         return (m, site_m) if peer else (self._reduce(m), None)
 
 
