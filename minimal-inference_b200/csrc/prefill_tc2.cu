@@ -20,12 +20,17 @@
 //               one tile's softmax warps work on S, the pipe works for the
 //               other tile;
 //   warps 2-5   softmax of tile A, warps 6-9 softmax of tile B: thread = TMEM
-//               lane = packed row, the whole 128-key row of S in two passes
-//               over TMEM (row max; then exp2, row sum, 16-bit P written
-//               over the S columns it came from), O rescaled in TMEM only
-//               when a row max grows by more than 2^8;
+//               lane = packed row, the whole 128-key row of S. After an
+//               item's first tile in one pass over TMEM against the running
+//               max (exp2, row sum, 16-bit P written over the S columns it
+//               came from); the first tile, and any tile whose max grows by
+//               more than 2^8, in two (row max first); O rescaled in TMEM
+//               only then;
 //   warps 10-13 epilogue: normalise a finished item's O_A and O_B and store
 //               them, releasing each O buffer as soon as it is read.
+// An item's last tile is a half tile when at most 64 of its keys are visible
+// to the item's rows (causal diagonal, ragged end): its products cover those
+// 64 keys only (QK^T with N = 64, P V over 4 key steps).
 // TMEM (512 columns): S_A [0,128), S_B [128,256) with P_A / P_B in their
 // first 64 columns; O_A and O_B (head_dim columns each) from column 256.
 // Every wait is bounded; TMEM is freed on every path.
@@ -57,7 +62,7 @@ template <int D> struct Pf2Layout {
   static constexpr int ITEM_OFF = BAR_OFF + 320;       // 2 work-item records
   // hand-off to the epilogue, per slot (item parity) and tile: row sums,
   // row maxima; per slot the output record
-  static constexpr int LSUM_OFF = ITEM_OFF + 64;
+  static constexpr int LSUM_OFF = ITEM_OFF + 2 * 48;
   static constexpr int MFIN_OFF = LSUM_OFF + 2 * 2 * kM * 4;
   static constexpr int EREC_OFF = MFIN_OFF + 2 * 2 * kM * 4;
   static constexpr int META_OFF = EREC_OFF + 2 * 16;
@@ -72,6 +77,8 @@ template <int D> struct Pf2Layout {
 struct __align__(16) Pf2Item {
   int b, h, t0, n_tiles;  // b < 0: no more items
   int q_start, lq, lk, page_base;
+  int last_keys;          // keys of the last tile visible to some row of the item
+  int pad[3];
 };
 
 template <typename T, int D>
@@ -187,7 +194,7 @@ __global__ void __launch_bounds__(kThreads2, 1)
         k_ahead = -1;
       }
       k = __shfl_sync(0xffffffffu, k, 0);
-      Pf2Item rec{-1, 0, 0, 0, 0, 0, 0, 0};
+      Pf2Item rec{-1, 0, 0, 0, 0, 0, 0, 0, 0, {0, 0, 0}};
       if (k < n_items) {
         int lo = 0, hi = p.batch - 1;  // last b with tiles_pre[b] * hkv <= k
         while (lo < hi) {
@@ -207,6 +214,7 @@ __global__ void __launch_bounds__(kThreads2, 1)
         const int lim_tok =
             p.causal ? min(rec.lk, rec.lk - rec.lq + rec.t0 + rows_tok) : rec.lk;
         rec.n_tiles = lim_tok > 0 ? cdiv(lim_tok, kN) : 0;
+        rec.last_keys = lim_tok - (rec.n_tiles - 1) * kN;
       }
       const int slot = it & 1;
       if (it >= 2 &&
@@ -255,12 +263,15 @@ __global__ void __launch_bounds__(kThreads2, 1)
             !__all_sync(0xffffffffu, mbar_wait_bounded(empty, ((gtile / nst) - 1) & 1)))
           return false;
         const int tok_tile = j * kN;
-        const int nvc = min(8, cdiv(rec.lk - tok_tile, 16));
+        // 16-token chunks up to the item's last visible key. Past it no row
+        // sees a key: every warp masks those S columns (P = 0), and a half
+        // tile's products do not reach them.
+        const int nvc = min(8, cdiv((j + 1 == rec.n_tiles ? rec.last_keys : kN), 16));
         unsigned char *base = smem + (which ? L::V_OFF + st * L::V_BYTES : L::K_OFF + st * L::K_BYTES);
         if (which == 1 && gtile < L::NV && nvc < 8) {
-          // V chunks past the request's end are multiplied by P = 0; on a
-          // stage's first use they hold whatever shared memory held, so zero
-          // them (later uses keep an earlier tile's finite values there)
+          // V chunks not loaded are multiplied by P = 0; on a stage's first
+          // use they hold whatever shared memory held, so zero them (later
+          // uses keep an earlier tile's finite values there)
           for (int dh = 0; dh < DH; ++dh) {
             uint4 *v = reinterpret_cast<uint4 *>(base + dh * (kN * 128) + nvc * 16 * 128);
             for (int i = lane; i < (8 - nvc) * 16 * 128 / 16; i += 32) v[i] = make_uint4(0, 0, 0, 0);
@@ -312,9 +323,12 @@ __global__ void __launch_bounds__(kThreads2, 1)
     if (lane == 0) {
       const uint32_t fmt = std::is_same<T, __nv_bfloat16>::value ? 1u : 0u;
       const uint32_t idesc_qk = umma_idesc(fmt, false, kN, kM);
+      const uint32_t idesc_qk_half = umma_idesc(fmt, false, kN / 2, kM);
       const uint32_t idesc_pv = umma_idesc(fmt, true, D, kM);
-      // S_x = Q_x K^T of global tile t (K stage t % NK)
-      auto issue_qk = [&](int t, int x) {
+      // S_x = Q_x K^T of global tile t (K stage t % NK); a half tile (the
+      // item's last, with at most kN / 2 visible keys) computes its first
+      // kN / 2 columns only
+      auto issue_qk = [&](int t, int x, bool half) {
         const uint32_t q_addr = smem_u32(smem + L::Q_OFF + x * L::Q_BYTES);
         const uint32_t k_addr = smem_u32(smem + L::K_OFF + (t % L::NK) * L::K_BYTES);
 #pragma unroll
@@ -322,19 +336,21 @@ __global__ void __launch_bounds__(kThreads2, 1)
           const uint32_t off = (kk >> 2) * (kM * 128) + (kk & 3) * 32;
           const uint32_t koff = (kk >> 2) * (kN * 128) + (kk & 3) * 32;
           umma(tmem + L::S_COL + x * kN, umma_desc(q_addr + off, 16, 1024),
-               umma_desc(k_addr + koff, 16, 1024), idesc_qk, kk > 0);
+               umma_desc(k_addr + koff, 16, 1024), half ? idesc_qk_half : idesc_qk, kk > 0);
         }
         umma_commit(&s_full[x]);
       };
       // O_x (+)= P_x V of global tile t (V stage t % NV); P from TMEM (16
       // keys = 8 columns per step), V MN-major: 64-wide d blocks kN*128
-      // bytes apart, 8-token groups 1 KB apart
-      auto issue_pv = [&](int t, int x, bool acc) {
+      // bytes apart, 8-token groups 1 KB apart; a half tile's first kN / 2
+      // keys only
+      auto issue_pv = [&](int t, int x, bool acc, bool half) {
         const uint32_t v_addr = smem_u32(smem + L::V_OFF + (t % L::NV) * L::V_BYTES);
 #pragma unroll
         for (int kk = 0; kk < kN / 16; ++kk)
-          umma_ts(tmem + L::O_COL + x * D, tmem + L::S_COL + x * kN + kk * 8,
-                  umma_desc(v_addr + kk * 16 * 128, kN * 128, 1024), idesc_pv, acc || kk > 0);
+          if (!half || kk < kN / 32)
+            umma_ts(tmem + L::O_COL + x * D, tmem + L::S_COL + x * kN + kk * 8,
+                    umma_desc(v_addr + kk * 16 * 128, kN * 128, 1024), idesc_pv, acc || kk > 0);
         umma_commit(&pv_done[x]);
       };
       int gt = 0, oc = 0;
@@ -347,6 +363,7 @@ __global__ void __launch_bounds__(kThreads2, 1)
         if (rec.b < 0) break;
         const int n = rec.n_tiles;
         if (n == 0) continue;
+        const bool half_last = rec.last_keys <= kN / 2;  // the last tile is a half tile
         // first products of the item: S_A(0), S_B(0)
         for (int x = 0; x < 2 && ok; ++x) {
           if (!mbar_wait_bounded(&q_full[x], oc & 1) ||
@@ -355,7 +372,7 @@ __global__ void __launch_bounds__(kThreads2, 1)
             break;
           }
           tc_fence_after();
-          issue_qk(gt, x);
+          issue_qk(gt, x, n == 1 && half_last);
           issued = true;
           if (n == 1) umma_commit(&q_empty[x]);
         }
@@ -373,7 +390,7 @@ __global__ void __launch_bounds__(kThreads2, 1)
               break;
             }
             tc_fence_after();
-            issue_pv(t, x, j > 0);
+            issue_pv(t, x, j > 0, j + 1 == n && half_last);
             if (x == 1) umma_commit(&v_empty[t % L::NV]);
             if (j + 1 == n) umma_commit(&o_full[x]);
             if (j + 1 < n) {
@@ -384,7 +401,7 @@ __global__ void __launch_bounds__(kThreads2, 1)
                 break;
               }
               tc_fence_after();
-              issue_qk(t + 1, x);
+              issue_qk(t + 1, x, j + 2 == n && half_last);
               if (x == 1) umma_commit(&k_empty[(t + 1) % L::NK]);
               if (j + 2 == n) umma_commit(&q_empty[x]);  // the item's last QK^T of tile x
             }
@@ -462,46 +479,81 @@ __global__ void __launch_bounds__(kThreads2, 1)
         if (!__all_sync(0xffffffffu, mbar_wait_bounded(&s_full[x], gt & 1))) { ok = false; break; }
         tc_fence_after();
         const int kbase = j * kN;
-        const bool masked = __any_sync(0xffffffffu, kbase + kN > lim);
-        // pass 1: the row max over the tile's keys (raw scores; the scale is
-        // folded into the exponent's FMA)
-        float mt = -INFINITY;
-#pragma unroll 1
-        for (int c = 0; c < kN / 32; ++c) {
-          float sv[32];
+        // columns of S this tile computed: kN / 2 for a half tile (the
+        // item's last, with at most kN / 2 visible keys)
+        const int ncol = (j + 1 == rec.n_tiles && rec.last_keys <= kN / 2) ? kN / 2 : kN;
+        const bool masked = __any_sync(0xffffffffu, kbase + ncol > lim);
+        // S chunk c (32 keys) into registers, keys at or past lim as -inf
+        auto load_chunk = [&](int c, float *sv) {
           tmem_ld32(tmem_s + c * 32, sv);
           tmem_wait_ld();
           if (masked) {
 #pragma unroll
             for (int i = 0; i < 32; ++i) sv[i] = (kbase + c * 32 + i < lim) ? sv[i] : -INFINITY;
           }
-#pragma unroll
-          for (int i = 0; i < 32; ++i) mt = fmaxf(mt, sv[i]);
-        }
-        mt *= p.scale_log2;  // scale_log2 > 0: the max commutes with it
-        // keep the old max unless this tile's exceeds it by > kRescaleLog2
-        const float m_new = (mt > m + kRescaleLog2 || m == -INFINITY) ? fmaxf(m, mt) : m;
-        const float ms = m_new == -INFINITY ? 0.f : m_new;
-        const float corr = m == m_new ? 1.f : fast_exp2(m - ms);
-        // pass 2: P = 2^(s * scale - m) as 16-bit pairs over the S columns
-        // already read (chunk c's P lands in columns [16 c, 16 c + 16))
-        float sum = 0.f;
+        };
+        float corr = 1.f, sum = 0.f, m_new = m;
+        bool fast = false;
+        if (j > 0) {
+          // one pass against the running max m: P = 2^(s * scale - m), right
+          // unless a key of this tile exceeds m + kRescaleLog2 (then the two
+          // passes below redo the tile). The row max and the row sum run in
+          // four independent chains each, off the exponentials' path.
+          const float ms = m == -INFINITY ? 0.f : m;  // a row with no key yet
+          float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+          float sm[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll 1
-        for (int c = 0; c < kN / 32; ++c) {
-          float sv[32];
-          tmem_ld32(tmem_s + c * 32, sv);
-          tmem_wait_ld();
-          uint32_t pk[16];
+          for (int c = 0; c < ncol / 32; ++c) {
+            float sv[32];
+            load_chunk(c, sv);
+            uint32_t pk[16];
 #pragma unroll
-          for (int i = 0; i < 32; i += 2) {
-            const bool in0 = !masked || kbase + c * 32 + i < lim;
-            const bool in1 = !masked || kbase + c * 32 + i + 1 < lim;
-            const float p0 = in0 ? fast_exp2(fmaf(sv[i], p.scale_log2, -ms)) : 0.f;
-            const float p1 = in1 ? fast_exp2(fmaf(sv[i + 1], p.scale_log2, -ms)) : 0.f;
-            sum += p0 + p1;
-            pk[i >> 1] = Pack2<T>::run(p0, p1);
+            for (int i = 0; i < 32; i += 2) {
+              mx[(i >> 1) & 3] = max3f(mx[(i >> 1) & 3], sv[i], sv[i + 1]);
+              const float p0 = fast_exp2(fmaf(sv[i], p.scale_log2, -ms));  // 2^-inf = 0
+              const float p1 = fast_exp2(fmaf(sv[i + 1], p.scale_log2, -ms));
+              sm[(i >> 1) & 3] += p0 + p1;
+              pk[i >> 1] = Pack2<T>::run(p0, p1);
+            }
+            tmem_st16(tmem_s + c * 16, pk);  // columns [16 c, 16 c + 16): read already
           }
-          tmem_st16(tmem_s + c * 16, pk);
+          const float mt = max3f(mx[0], mx[1], fmaxf(mx[2], mx[3])) * p.scale_log2;
+          sum = (sm[0] + sm[1]) + (sm[2] + sm[3]);
+          fast = __all_sync(0xffffffffu, !(mt > m + kRescaleLog2));
+        }
+        if (!fast) {
+          // pass 1: the row max over the tile's keys (raw scores; the scale
+          // is folded into the exponent's FMA)
+          float mt = -INFINITY;
+#pragma unroll 1
+          for (int c = 0; c < ncol / 32; ++c) {
+            float sv[32];
+            load_chunk(c, sv);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) mt = fmaxf(mt, sv[i]);
+          }
+          mt *= p.scale_log2;  // scale_log2 > 0: the max commutes with it
+          // keep the old max unless this tile's exceeds it by > kRescaleLog2
+          m_new = (mt > m + kRescaleLog2 || m == -INFINITY) ? fmaxf(m, mt) : m;
+          const float ms = m_new == -INFINITY ? 0.f : m_new;
+          corr = m == m_new ? 1.f : fast_exp2(m - ms);
+          // pass 2: P = 2^(s * scale - m) as 16-bit pairs over the S columns
+          // already read (chunk c's P lands in columns [16 c, 16 c + 16))
+          sum = 0.f;
+#pragma unroll 1
+          for (int c = 0; c < ncol / 32; ++c) {
+            float sv[32];
+            load_chunk(c, sv);
+            uint32_t pk[16];
+#pragma unroll
+            for (int i = 0; i < 32; i += 2) {
+              const float p0 = fast_exp2(fmaf(sv[i], p.scale_log2, -ms));
+              const float p1 = fast_exp2(fmaf(sv[i + 1], p.scale_log2, -ms));
+              sum += p0 + p1;
+              pk[i >> 1] = Pack2<T>::run(p0, p1);
+            }
+            tmem_st16(tmem_s + c * 16, pk);
+          }
         }
         l = l * corr + sum;
         m = m_new;

@@ -105,6 +105,13 @@ __device__ __forceinline__ float fast_exp2(float x) {
   return y;
 }
 
+// max(a, b, c) in one instruction (sm_100 three-input max).
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+  float m;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(m) : "f"(a), "f"(b), "f"(c));
+  return m;
+}
+
 // A row's running max moves only when a tile's max exceeds it by more than
 // this (log2 units): until then P = 2^(s - m) stays below 2^8, exact enough
 // in bf16/fp16 and far from overflow in the fp32 sums, and O needs no rescale.
