@@ -9,9 +9,10 @@ synchronisation steps in program order:
 * ``("tma", bar)``        an asynchronous copy that completes on ``bar``
                           at any later time, in any order;
 * ``("mma", tag)``        a tensor-core product, and
-* ``("commit", bar)``     an arrival on ``bar`` once every product issued
-                          before it has completed (products complete in
-                          issue order).
+* ``("commit", bar)``     an arrival on ``bar`` once every product the same
+                          role issued before it has completed (each role's
+                          products complete in its issue order; two roles'
+                          products in any interleaving).
 
 ``run`` interleaves the roles and the asynchronous completions at random.
 It raises ``AssertionError`` on a deadlock (nothing can move), on a wait
@@ -39,11 +40,12 @@ class Bar:
 def run(bars: dict, roles: dict, seed: int, max_steps: int = 10 ** 6) -> None:
     rnd = random.Random(seed)
     pending = []     # barriers with an asynchronous copy in flight
-    products = []    # in-order tensor-core queue: ("mma", tag) / ("commit", bar)
+    products = {}    # per issuing role, in order: ("mma", tag) / ("commit", bar)
     action = {name: None for name in roles}
     alive = set(roles)
     for _ in range(max_steps):
-        if not (alive or pending or products):
+        queues = [q for q in products.values() if q]
+        if not (alive or pending or queues):
             return
         progress = False
         order = sorted(alive)
@@ -74,7 +76,7 @@ def run(bars: dict, roles: dict, seed: int, max_steps: int = 10 ** 6) -> None:
                 elif kind == "tma":
                     pending.append(act[1])
                 else:
-                    products.append(act)
+                    products.setdefault(name, []).append(act)
                 act, progress = None, True
                 if rnd.random() < 0.3:
                     break
@@ -82,11 +84,12 @@ def run(bars: dict, roles: dict, seed: int, max_steps: int = 10 ** 6) -> None:
         if pending and rnd.random() < 0.5:
             bars[pending.pop(rnd.randrange(len(pending)))].arrive()
             progress = True
-        if products and rnd.random() < 0.5:
-            act = products.pop(0)
+        queues = [q for q in products.values() if q]
+        if queues and rnd.random() < 0.5:
+            act = rnd.choice(queues).pop(0)
             if act[0] == "commit":
                 bars[act[1]].arrive()
             progress = True
-        if not progress and not pending and not products:
+        if not progress and not pending and not any(products.values()):
             raise AssertionError(f"deadlock: {({n: action[n] for n in alive})}")
     raise AssertionError("no end within the step limit")
