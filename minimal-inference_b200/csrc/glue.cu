@@ -35,6 +35,7 @@ template <typename T, int V>
 __global__ void __launch_bounds__(1024) add_rmsnorm_vec_kernel(
     const T *__restrict__ x, T *__restrict__ residual, const T *__restrict__ w, T *__restrict__ y,
     int hidden, float eps, int has_x) {
+  pdl_trigger();  // a programmatic-dependent successor waits for this grid itself
   __shared__ float s_part[32];
   const int nvec = hidden >> 3;
   const int64_t base = static_cast<int64_t>(blockIdx.x) * hidden;
@@ -89,6 +90,7 @@ template <typename T>
 __global__ void __launch_bounds__(256) add_rmsnorm_kernel(
     const T *__restrict__ x, T *__restrict__ residual, const T *__restrict__ w, T *__restrict__ y,
     int hidden, float eps, int has_x) {
+  pdl_trigger();  // a programmatic-dependent successor waits for this grid itself
   __shared__ float s_part[32];
   const int64_t base = static_cast<int64_t>(blockIdx.x) * hidden;
   T *rr = residual + base;
@@ -119,6 +121,7 @@ __device__ __forceinline__ T silu_mul_one(T g, T u) {
 template <typename T, int VEC>
 __global__ void __launch_bounds__(256) silu_mul_kernel(const T *__restrict__ gu, T *__restrict__ out,
                                                        int rows, int inter) {
+  pdl_trigger();  // a programmatic-dependent successor waits for this grid itself
   const int per_row = inter / VEC;
   const int64_t n = static_cast<int64_t>(rows) * per_row;
   for (int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; idx < n;

@@ -11,7 +11,9 @@
 // thread-block cluster, each leaves its fp32 partial in its own shared
 // memory, and after a cluster barrier each sums its share of the rows over
 // all ranks' partials in rank order (distributed shared memory), so the
-// result does not depend on which split finished first.
+// result does not depend on which split finished first. Launched as a
+// programmatic dependent: the first stages of W (which no kernel writes) are
+// requested before the wait for the predecessor, only X after it.
 // 192 threads: warp 0 TMA producer, warp 1 MMA issuer (one thread),
 // warps 2-5 epilogue (thread = TMEM lane = output column).
 #include <algorithm>
@@ -47,11 +49,15 @@ __device__ __forceinline__ void cluster_sync_all() {
                    "memory");
 }
 
-__device__ __forceinline__ float ld_cluster_f32(uint32_t local_addr, uint32_t rank) {
+// 16 bytes at the same shared-memory offset in cluster rank `rank`
+__device__ __forceinline__ float4 ld_cluster_v4(uint32_t local_addr, uint32_t rank) {
   uint32_t remote;
-  float v;
+  float4 v;
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(local_addr), "r"(rank));
-  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(remote) : "memory");
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(remote)
+               : "memory");
   return v;
 }
 
@@ -102,9 +108,19 @@ __global__ void __launch_bounds__(kPThreads, 2)
     // ============================ producer ==================================
     if (lane == 0) {
       const uint64_t pol_w = evict_first_policy(), pol_x = evict_last_policy();
-      for (int i = 0; i < nk; ++i) {
+      // the first stages' W before the predecessor is waited for; X (its
+      // output) after
+      const int npre = min(nk, kPStages);
+      for (int i = 0; i < npre; ++i) {
+        mbar_arrive_expect_tx(&full[i], kPWBytes + kPXBytes);
+        tma_load_3d(sw + i * kPWBytes, &wmap, (k0 + i) * kPBK, 0, nb * kPBN, &full[i], pol_w);
+      }
+      pdl_wait();
+      for (int i = 0; i < npre; ++i)
+        tma_load_3d(sx + i * kPXBytes, &xmap, (k0 + i) * kPBK, 0, 0, &full[i], pol_x);
+      for (int i = npre; i < nk; ++i) {
         const int st = i % kPStages;
-        if (i >= kPStages && !mbar_wait_bounded(&empty[st], ((i / kPStages) - 1) & 1)) {
+        if (!mbar_wait_bounded(&empty[st], ((i / kPStages) - 1) & 1)) {
           ok = false;
           break;
         }
@@ -148,6 +164,7 @@ __global__ void __launch_bounds__(kPThreads, 2)
     const int cl = qd * 32 + lane;  // column in the block = TMEM lane
     const uint32_t taddr = tmem + (static_cast<uint32_t>(qd * 32) << 16);
     if (!__all_sync(0xffffffffu, mbar_wait_bounded(done, 0))) ok = false;
+    pdl_wait();  // (returns at once: the producer has waited) y is written below
     tc_fence_after();
     tmem_ld32(taddr, v);
     tmem_wait_ld();
@@ -170,18 +187,36 @@ __global__ void __launch_bounds__(kPThreads, 2)
   if (p.splits > 1) {
     cluster_sync_all();  // every rank's partial is in its shared memory
     if (warp >= 2) {
-      // this rank's rows: split, split + splits, ...; the sum over ranks in
-      // rank order
-      const int cl = (warp & 3) * 32 + lane;
-      const int col = nb * kPBN + cl;
-      if (col < p.n) {
-        const float b = p.bias ? Elt<T>::to(static_cast<const T *>(p.bias)[col]) : 0.f;
-        T *y = static_cast<T *>(p.y);
-        for (int r = split; r < p.m; r += p.splits) {
-          const uint32_t a = smem_u32(part + r * kPBN + cl);
-          float acc = 0.f;
-          for (int q = 0; q < p.splits; ++q) acc += ld_cluster_f32(a, static_cast<uint32_t>(q));
-          y[static_cast<int64_t>(r) * p.ldy + col] = Elt<T>::from(acc + b);
+      // this rank's rows: split, split + splits, ...; a thread takes 4
+      // columns of every 4th of them and sums the ranks' partials in rank
+      // order (all ranks' 16-byte loads in flight first)
+      const int t = threadIdx.x - 64;
+      const int c4 = (t & 31) * 4, sub = t >> 5;
+      const int col0 = nb * kPBN + c4;
+      T *y = static_cast<T *>(p.y);
+      for (int r = split + sub * p.splits; r < p.m; r += 4 * p.splits) {
+        const uint32_t a = smem_u32(part + r * kPBN + c4);
+        float4 pv[kPMaxSplits];
+#pragma unroll
+        for (int q = 0; q < kPMaxSplits; ++q)
+          if (q < p.splits) pv[q] = ld_cluster_v4(a, static_cast<uint32_t>(q));
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int q = 0; q < kPMaxSplits; ++q)
+          if (q < p.splits) {
+            acc.x += pv[q].x;
+            acc.y += pv[q].y;
+            acc.z += pv[q].z;
+            acc.w += pv[q].w;
+          }
+        const float vals[4] = {acc.x, acc.y, acc.z, acc.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int col = col0 + e;
+          if (col < p.n) {
+            const float b = p.bias ? Elt<T>::to(static_cast<const T *>(p.bias)[col]) : 0.f;
+            y[static_cast<int64_t>(r) * p.ldy + col] = Elt<T>::from(vals[e] + b);
+          }
         }
       }
     }
@@ -196,6 +231,35 @@ __global__ void __launch_bounds__(kPThreads, 2)
   }
 }
 
+// Clusters of `size` CTAs of proj_kernel<T> resident at once on the current
+// device (cached per device and size; 0 if the query fails).
+template <typename T>
+int proj_max_clusters(int size) {
+  static std::atomic<int> cache[64][kPMaxSplits + 1];  // count + 1; 0: not queried
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev >= 64) return 0;
+  const int v = cache[dev][size].load();
+  if (v > 0) return v - 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(size * 64);
+  cfg.blockDim = dim3(kPThreads);
+  cfg.dynamicSmemBytes = kPSmem;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = size;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int num = 0;
+  if (cudaOccupancyMaxActiveClusters(&num, proj_kernel<T>, &cfg) != cudaSuccess) {
+    cudaGetLastError();
+    num = 0;
+  }
+  cache[dev][size].store(num + 1);
+  return num;
+}
+
 template <typename T>
 int launch_proj(const void *x, int64_t ldx, const void *w, int64_t ldw, const void *bias,
                 void *y, int64_t ldy, int m, int n, int k, int dtype, int32_t *status,
@@ -207,27 +271,37 @@ int launch_proj(const void *x, int64_t ldx, const void *w, int64_t ldw, const vo
                                 "row strides a multiple of 8 elements)");
   const int nblocks = (n + kPBN - 1) / kPBN;
   const int ksteps = k / kPBK;
-  // split K so that every SM streams (two CTAs per SM), at least 4 K steps
-  // (64 KB of W) per CTA, at most one cluster's worth of splits
-  const int slots = 2 * num_sms();
-  const int splits =
-      std::max(1, std::min({slots / nblocks, ksteps / 4, kPMaxSplits}));
   static std::atomic<unsigned long long> attr_set{0};
   if (smem_limit_once(attr_set, proj_kernel<T>, kPSmem) != cudaSuccess)
     return check_launch("proj_kernel smem attribute");
+  // K split: enough CTAs for two per SM, at most 8 (one cluster) and at
+  // least 4 K steps (64 KB of W) each; fewer when under 85 % of the
+  // clusters would be resident at once (then the most that all fit)
+  const int want = std::max(1, std::min({2 * num_sms() / nblocks, ksteps / 4, kPMaxSplits}));
+  int splits = want;
+  if (want > 1 && 100 * proj_max_clusters<T>(want) < 85 * nblocks) {
+    splits = 1;
+    for (int c = want - 1; c > 1; --c)
+      if (nblocks <= proj_max_clusters<T>(c)) {
+        splits = c;
+        break;
+      }
+  }
   ProjParams p{y, bias, status, m, n, k, static_cast<int>(ldy), splits, ksteps};
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(nblocks * splits);
   cfg.blockDim = dim3(kPThreads);
   cfg.dynamicSmemBytes = kPSmem;
   cfg.stream = s;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = splits;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   cudaLaunchKernelEx(&cfg, proj_kernel<T>, wmap, xmap, p);
   return check_launch("proj_kernel");
 }
