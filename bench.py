@@ -767,6 +767,119 @@ def run_prefill(args):
     print(json.dumps(line), flush=True)
 
 
+PROJ_SHAPES = {"qkv": (6144, 4096), "o_proj": (4096, 4096), "gate_up": (28672, 4096),
+               "down_proj": (4096, 14336), "lm_head": (32768, 4096)}  # Mistral-7B [N, K]
+
+
+def run_proj(args):
+    """``--workload proj``: the decode step's projections at 32 rows
+    (Mistral-7B shapes), this package's small-M projection kernel
+    (``glue.proj_small_m``) beside cuBLAS (``F.linear`` on the nn.Linear
+    layout and ``x @ Wt`` on the transposed one). Each measurement is 30
+    (add+RMSNorm -> projection) pairs captured in one CUDA graph, the order
+    of a decode step, over weight copies larger than L2 together, minus the
+    RMSNorm alone; CUDA events around 5 replays. ``--proj-shape`` limits the
+    run to one shape (for a profiler)."""
+    import torch
+    from mi_b200 import glue
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    m = 32
+
+    def graph_us(fns, reps=30):
+        for f in fns:
+            f()
+        torch.cuda.synchronize()
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            for f in fns:
+                f()
+        torch.cuda.current_stream().wait_stream(side)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            for i in range(reps):
+                fns[i % len(fns)]()
+        g.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(5):
+            g.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) * 1e3 / (5 * reps)
+
+    shapes = {args.proj_shape: PROJ_SHAPES[args.proj_shape]} if args.proj_shape else PROJ_SHAPES
+    out = {}
+    for name, (n, k) in shapes.items():
+        size = n * k * 2
+        copies = max(2, math.ceil(400e6 / size))
+        ws = [(torch.randn(n, k, device=dev) * 0.02).to(torch.bfloat16) for _ in range(copies)]
+        res = torch.randn(m, k, device=dev).to(torch.bfloat16)
+        nw = torch.ones(k, device=dev, dtype=torch.bfloat16)
+        xn = torch.empty(m, k, device=dev, dtype=torch.bfloat16)
+        y = torch.empty(m, n, device=dev, dtype=torch.bfloat16)
+
+        def norm():
+            glue.add_rmsnorm(None, res, nw, 1e-6, out=xn)
+        t_norm = graph_us([norm])
+        t_mi = graph_us([lambda w=w: (norm(), glue.proj_small_m(xn, w, out=y)) for w in ws]) - t_norm
+        row = {"mi_us": round(t_mi, 2), "mi_TBs": round(size / t_mi / 1e6, 2)}
+        if not args.proj_shape:
+            wts = [w.t().contiguous() for w in ws]
+            t_lin = graph_us([lambda w=w: (norm(), torch.nn.functional.linear(xn, w))
+                              for w in ws]) - t_norm
+            t_mm = graph_us([lambda w=w: (norm(), torch.mm(xn, w, out=y)) for w in wts]) - t_norm
+            row.update({"cublas_linear_us": round(t_lin, 2), "cublas_wt_us": round(t_mm, 2)})
+            del wts
+        out[name] = row
+        del ws
+        torch.cuda.empty_cache()
+    st = int(glue.proj_status(dev).item())
+    print(json.dumps({"workload": "proj", "rows": m, "dtype": "bf16", "shapes_NK": PROJ_SHAPES,
+                      "status": st, "results": out,
+                      "timing": "30 add+RMSNorm -> projection pairs per CUDA graph, minus the "
+                                "RMSNorm alone; weights cycled over copies larger than L2"}),
+          flush=True)
+
+
+def run_model_step(args):
+    """``--workload model-step``: config 3 (Mistral-7B shape, 32 requests)
+    stepped to a steady decode, then one decode step between
+    ``cudaProfilerStart`` / ``cudaProfilerStop`` (for a profiler's
+    ``--profile-from-start off``); prints the steady step times."""
+    import torch
+    from mi_b200.model import PRESETS, Model
+    from mi_b200.scheduler import Request, Scheduler
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    cfg = PRESETS["mistral-7b"]
+    model = Model.create(cfg, dev, torch.bfloat16, seed=3)
+    rng = np.random.default_rng(3)
+    lens = rng.integers(128, 1025, 32).tolist()
+    prompts = [rng.integers(0, cfg.vocab_size, n).tolist() for n in lens]
+    sched = Scheduler(model, cfg, dev, torch.bfloat16, max_batch_size=32,
+                      max_seq_len=1024 + 66, page_size=16, eos_token_ids=set())
+    for i, p in enumerate(prompts):
+        sched.submit_request(Request(f"r{i}", p, 40, 0.0))
+    for _ in range(10):
+        sched.step()
+    torch.cuda.synchronize()
+    times = []
+    for _ in range(5):
+        t0 = time.perf_counter()
+        sched.step()
+        torch.cuda.synchronize()
+        times.append(round((time.perf_counter() - t0) * 1e3, 3))
+    torch.cuda.profiler.start()
+    sched.step()
+    torch.cuda.synchronize()
+    torch.cuda.profiler.stop()
+    print(json.dumps({"workload": "model-step", "steady_decode_step_ms": times}), flush=True)
+
+
 def run_flashinfer_context(args):
     """Context, not a baseline arm: the reference's own GPU path for one
     config-2 layer on this GPU -- stock ``flashinfer.page.append_paged_kv_cache``
@@ -877,11 +990,13 @@ def parse_args():
                     help="skip the Mistral-7B-shape decode measurement (config 3)")
     ap.add_argument("--workload",
                     choices=["config2", "config1", "config4", "config5", "prefill",
-                             "decode-shapes", "flashinfer-context"],
+                             "decode-shapes", "flashinfer-context", "proj", "model-step"],
                     default="config2",
                     help="config5: Qwen2.5-72B tensor-parallel decode over the launch's GPUs; "
                          "prefill: the paged prefill kernel alone on config 3's prompts")
     ap.add_argument("--model", default=None, help="config5: model preset (default qwen2.5-72b)")
+    ap.add_argument("--proj-shape", choices=sorted(PROJ_SHAPES), default=None,
+                    help="proj: one projection shape only (no cuBLAS timings)")
     ap.add_argument("--batch", type=int, default=None,
                     help="config5: requests (default 64); config4: requests served (default 160)")
     ap.add_argument("--decode-steps", type=int, default=None,
@@ -1262,6 +1377,12 @@ def main():
         return
     if args.workload == "flashinfer-context":
         run_flashinfer_context(args)
+        return
+    if args.workload == "proj":
+        run_proj(args)
+        return
+    if args.workload == "model-step":
+        run_model_step(args)
         return
     import torch
     import torch.distributed as dist

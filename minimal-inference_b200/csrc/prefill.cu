@@ -9,7 +9,7 @@
 // This file holds the generic path: one warp per (query row, query head),
 // online softmax over the visible keys, any dtype (fp32 parity configs
 // included) and any head_dim <= 256. The tensor-core path lives in
-// prefill_tc.cu.
+// prefill_tc2.cu.
 #include "mi_common.cuh"
 #include "prefill.cuh"
 
@@ -141,10 +141,8 @@ extern "C" int mi_paged_prefill(
   if (workspace && workspace_bytes >= 256 && (reinterpret_cast<uintptr_t>(workspace) & 15) == 0)
     p.ctr = static_cast<unsigned *>(workspace);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  // tensor cores: two query tiles per work item, else one
-  int rc = launch_prefill_tc2(p, dtype, s);
-  if (rc >= 0) return rc;
-  rc = launch_prefill_tc(p, dtype, s);
+  // tensor cores (two query tiles per work item) where they cover the shape
+  const int rc = launch_prefill_tc2(p, dtype, s);
   if (rc >= 0) return rc;
   switch (dtype) {
     case MI_DTYPE_F32: return launch_generic<float>(p, s);

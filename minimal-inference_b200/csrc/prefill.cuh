@@ -1,5 +1,5 @@
 // Arguments shared by the generic (prefill.cu) and tensor-core
-// (prefill_tc.cu) paged prefill kernels.
+// (prefill_tc2.cu) paged prefill kernels.
 #pragma once
 
 #include "mi_common.cuh"
@@ -23,12 +23,9 @@ struct PrefillParams {
   unsigned *ctr;  // [2] work-item counters in the workspace (zero between calls), or null
 };
 
-// Tensor-core path (prefill_tc.cu). Returns -1 (nothing launched) when the
-// shape or layout is outside its coverage, so the caller runs the generic
-// kernel instead.
-int launch_prefill_tc(const PrefillParams &p, int dtype, cudaStream_t s);
-// Two query tiles per work item (prefill_tc2.cu), the same coverage; -1 when
-// outside it.
+// Tensor-core path (prefill_tc2.cu): two query tiles per work item. Returns
+// -1 (nothing launched) when the shape or layout is outside its coverage, so
+// the caller runs the generic kernel instead.
 int launch_prefill_tc2(const PrefillParams &p, int dtype, cudaStream_t s);
 
 }  // namespace mi

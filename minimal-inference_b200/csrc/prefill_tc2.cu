@@ -2,9 +2,10 @@
 // tcgen05 / TMEM, the softmax of one query tile running under the other's
 // tensor-core products.
 //
-// Same contract and coverage as prefill_tc.cu (the FlashInfer paged prefill
-// the reference runs, scheduler.py:530-534, :704-716, model.py:235): bf16 /
-// fp16, head_dim 64 / 128, page_size a multiple of 16. A work item is
+// Replaces the FlashInfer paged prefill the reference runs
+// (scheduler.py:530-534, :704-716, model.py:235) for bf16 / fp16, head_dim
+// 64 / 128, page_size a multiple of 16 (the generic kernel in prefill.cu
+// takes every other shape). A work item is
 // (request, KV head, 256 packed query rows): two query tiles A and B of 128
 // rows, a row being a (query token, query head of the GQA group) pair, so a
 // tile holds Tq = 128 / group tokens and every K/V tile brought in serves

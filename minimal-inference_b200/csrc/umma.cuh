@@ -1,4 +1,4 @@
-// tcgen05 / TMEM helpers shared by the tensor-core prefill kernels (sm_100a):
+// tcgen05 / TMEM helpers of the tensor-core kernels (prefill, projections; sm_100a):
 // shared-memory and instruction descriptors, MMA issue and commit, TMEM
 // loads and stores, the fast exp2 and 16-bit packing.
 #pragma once
