@@ -624,11 +624,7 @@ __global__ void __launch_bounds__(kThreads2, 1)
         const float inv = l > 0.f ? 1.f / l : 0.f;
         T *o = static_cast<T *>(p.out) + orow * D;
         const uint32_t tmem_o = tmem + L::O_COL + x * D + lane_base;
-#pragma unroll
-        for (int c = 0; c < D / 32; ++c) {
-          float ov[32];
-          tmem_ld32(tmem_o + c * 32, ov);
-          tmem_wait_ld();
+        auto store_chunk = [&](int c, const float *ov) {
           if (row_ok) {
 #pragma unroll
             for (int i = 0; i < 32; i += 8) {
@@ -640,14 +636,26 @@ __global__ void __launch_bounds__(kThreads2, 1)
               *reinterpret_cast<uint4 *>(o + c * 32 + i) = w;
             }
           }
+        };
+        // O in pairs of 32-column chunks, one TMEM round trip per pair; the
+        // O buffer goes back to the MMA as soon as its last pair is read
+#pragma unroll
+        for (int c = 0; c < D / 32; c += 2) {
+          float oa[32], ob[32];
+          tmem_ld32(tmem_o + c * 32, oa);
+          tmem_ld32(tmem_o + (c + 1) * 32, ob);
+          tmem_wait_ld();
+          if (c + 2 == D / 32) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&o_free[x]);  // O_x may be overwritten
+          }
+          store_chunk(c, oa);
+          store_chunk(c + 1, ob);
         }
         if (row_ok && p.lse) p.lse[orow] = l > 0.f ? (m + __log2f(l)) * kLn2 : -INFINITY;
-        tc_fence_before();
         __syncwarp();
-        if (lane == 0) {
-          mbar_arrive(&o_free[x]);             // O_x may be overwritten
-          mbar_arrive(&h_free[slot * 2 + x]);  // the hand-off slot may be rewritten
-        }
+        if (lane == 0) mbar_arrive(&h_free[slot * 2 + x]);  // the hand-off slot may be rewritten
       }
       if (!ok || er.x < 0) break;
     }
