@@ -49,6 +49,13 @@ REPO = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, os.path.join(REPO, "minimal-inference_b200"))
 sys.path.insert(0, REPO)
 
+# Under torchrun: NCCL's communicator-init log (ranks, devices, transports)
+# on stderr, set before torch loads NCCL; stdout keeps the one JSON line.
+if int(os.environ.get("WORLD_SIZE", "1")) > 1:
+    os.environ["NCCL_DEBUG"] = "INFO"
+    os.environ["NCCL_DEBUG_SUBSYS"] = "INIT"
+    os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
+
 METRIC = "paged decode attn HBM GB/s (% of peak); Mistral-7B-shape decode tok/s @B=32"
 CFG = dict(batch=32, hq=32, hkv=8, head_dim=128, page_size=16, ctx_lo=256, ctx_hi=4096,
            num_pages=10240, layers=32, seed=0)
@@ -464,13 +471,11 @@ def run_tp_decode(args):
     """``--workload config5``: ``tp_decode`` at the launch's N on its own."""
     import torch
     import torch.distributed as dist
-    from datetime import timedelta
 
     rank, world, local = dist_env()
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
-    if world > 1:
-        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+    active = nccl_group(dev, 300) if world > 1 else 1
     batch, steps = args.batch or 64, args.decode_steps or 128
     r = tp_decode(args, rank, world, local, dev, batch=batch, steps=steps,
                   allreduce=args.allreduce, name=args.model)
@@ -480,6 +485,7 @@ def run_tp_decode(args):
         return
     line = {
         "metric": r["metric"], "value": r["t2t_tok_s"], "unit": "tok/s", "n_gpus": world,
+        "gpus_active": active,
         "steps": steps, "warmup": 0, "ms_per_step": r["decode_step_ms"], "t2t_ms": r["t2t_ms"],
         "decode_step_tok_s": r["value"], "t2t_note": r["t2t_note"],
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
@@ -1008,6 +1014,20 @@ def parse_args():
     return ap.parse_args()
 
 
+def nccl_group(dev, timeout_s: int):
+    """The NCCL process group for N > 1 ranks (its init log is switched on
+    at the top of this file) and the number of distinct GPUs taking part
+    (device UUIDs gathered from every rank)."""
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+    dist.init_process_group("nccl", timeout=timedelta(seconds=timeout_s), device_id=dev)
+    uuid = str(torch.cuda.get_device_properties(dev).uuid)
+    uuids = [None] * dist.get_world_size()
+    dist.all_gather_object(uuids, uuid)
+    return len(set(uuids))
+
+
 def dist_env():
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -1386,13 +1406,11 @@ def main():
         return
     import torch
     import torch.distributed as dist
-    from datetime import timedelta
 
     rank, world, local = dist_env()
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
-    if world > 1:
-        dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=dev)
+    active = nccl_group(dev, 180) if world > 1 else 1
     heads = world > 1 and args.shard != "replicas"
     if heads and CFG["hkv"] % world:
         raise SystemExit(f"head sharding needs {CFG['hkv']} KV heads divisible by {world}")
@@ -1434,7 +1452,7 @@ def main():
         return
     line = {
         "metric": METRIC, "value": round(r["value"], 2), "unit": "GB/s", "n_gpus": world,
-        "steps": r["K"], "warmup": max(args.warmup, 3), "ms_per_step": round(r["ms_per_step"], 4),
+        "gpus_active": active, "steps": r["K"], "warmup": max(args.warmup, 3), "ms_per_step": round(r["ms_per_step"], 4),
         "higher_is_better": True, "scaling": "strong" if heads else "weak",
         "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic", "config": workload_config("heads" if heads else "replicas", world),
