@@ -25,6 +25,9 @@ SHAPES = [  # (m, n, k, bias)
     (16, 896, 4864, False),     # Qwen2.5-0.5B down_proj
     (5, 1000, 128, True),       # last 128-column block partial
     (32, 64, 64, False),        # one block, one K step
+    (17, 1001, 2048, True),     # odd column count: the reduction's 4-column groups end mid-group
+    (1, 4608, 3584, True),      # Qwen2.5-7B QKV (bias), one row
+    (32, 3584, 18944, False),   # Qwen2.5-7B down_proj
 ]
 
 
