@@ -49,6 +49,7 @@ constexpr int kM = 128;         // packed query rows per tile
 constexpr int kN = 128;         // KV tokens per tile
 constexpr int kThreads2 = 448;  // producer, MMA, 2 x 4 softmax warps, 4 epilogue warps
 constexpr int kMaxBatch2 = 1024;
+constexpr int kSortBatch = 128;  // requests ordered by length up to this batch
 
 template <int D> struct Pf2Layout {
   static constexpr int DH = D / 64;                 // 64-wide blocks of head_dim
@@ -67,8 +68,9 @@ template <int D> struct Pf2Layout {
   static constexpr int MFIN_OFF = LSUM_OFF + 2 * 2 * kM * 4;
   static constexpr int EREC_OFF = MFIN_OFF + 2 * 2 * kM * 4;
   static constexpr int META_OFF = EREC_OFF + 2 * 16;
-  // item prefix, qo_indptr, kv_indptr [batch+1] and kv_len [batch]
-  static constexpr int META_INTS = 4 * (kMaxBatch2 + 1);
+  // item prefix, qo_indptr, kv_indptr [batch+1], kv_len [batch] and the
+  // request order [batch]
+  static constexpr int META_INTS = 5 * (kMaxBatch2 + 1);
   static constexpr int SMEM = META_OFF + META_INTS * 4 + 1024;
   static constexpr int S_COL = 0;      // S_A at 0, S_B at kN (P over the first kN / 2)
   static constexpr int O_COL = 2 * kN; // O_A, O_B: D columns each
@@ -110,6 +112,7 @@ __global__ void __launch_bounds__(kThreads2, 1)
   int *s_qo = tiles_pre + (kMaxBatch2 + 1);
   int *s_ip = s_qo + (kMaxBatch2 + 1);
   int *s_lk = s_ip + (kMaxBatch2 + 1);
+  int *s_order = s_lk + (kMaxBatch2 + 1);  // work-item order of the requests
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = p.group;
@@ -130,12 +133,31 @@ __global__ void __launch_bounds__(kThreads2, 1)
     s_ip[i] = p.indptr[i];
     if (i < p.batch) s_lk[i] = kv_len_of(p.indptr, p.last, i, p.ps);
   }
-  if (warp == 0) {  // tiles_pre[i] = sum over b < i of ceil(qo_len_b / (2 Tq))
+  __syncthreads();
+  // Requests in decreasing query length (ties by index), so the queue ends
+  // with the shortest requests' light items and the CTAs finish together
+  // (rank by counting: batch^2 / blockDim comparisons per thread, so only up
+  // to kSortBatch requests; larger batches keep their order).
+  for (int i = threadIdx.x; i < p.batch; i += blockDim.x) {
+    int rank = i;
+    if (p.batch <= kSortBatch) {
+      const int li = s_qo[i + 1] - s_qo[i];
+      rank = 0;
+      for (int j = 0; j < p.batch; ++j) {
+        const int lj = s_qo[j + 1] - s_qo[j];
+        rank += (lj > li || (lj == li && j < i)) ? 1 : 0;
+      }
+    }
+    s_order[rank] = i;
+  }
+  __syncthreads();
+  if (warp == 0) {  // tiles_pre[i] = sum over the first i requests in s_order of ceil(qo_len / (2 Tq))
     int carry = 0;
     if (lane == 0) tiles_pre[0] = 0;
     for (int base = 0; base < p.batch; base += 32) {
       const int bb = base + lane;
-      int x = bb < p.batch ? cdiv(max(0, qo_at(bb + 1) - qo_at(bb)), tq2) : 0;
+      const int rb = bb < p.batch ? s_order[bb] : 0;
+      int x = bb < p.batch ? cdiv(max(0, s_qo[rb + 1] - s_qo[rb]), tq2) : 0;
 #pragma unroll
       for (int o = 1; o < 32; o <<= 1) {
         const int y = __shfl_up_sync(0xffffffffu, x, o);
@@ -197,13 +219,13 @@ __global__ void __launch_bounds__(kThreads2, 1)
       k = __shfl_sync(0xffffffffu, k, 0);
       Pf2Item rec{-1, 0, 0, 0, 0, 0, 0, 0, 0, {0, 0, 0}};
       if (k < n_items) {
-        int lo = 0, hi = p.batch - 1;  // last b with tiles_pre[b] * hkv <= k
+        int lo = 0, hi = p.batch - 1;  // last position with tiles_pre[pos] * hkv <= k
         while (lo < hi) {
           const int mid = (lo + hi + 1) >> 1;
           if (tiles_pre[mid] * p.hkv <= k) lo = mid; else hi = mid - 1;
         }
-        const int b = lo, ntq = tiles_pre[b + 1] - tiles_pre[b];
-        const int rem = k - tiles_pre[b] * p.hkv;
+        const int b = s_order[lo], ntq = tiles_pre[lo + 1] - tiles_pre[lo];
+        const int rem = k - tiles_pre[lo] * p.hkv;
         rec.b = b;
         rec.h = rem / ntq;
         rec.t0 = (ntq - 1 - rem % ntq) * tq2;
