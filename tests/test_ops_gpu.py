@@ -452,6 +452,35 @@ def test_prefill_repeated_calls_share_workspace(ws_bytes):
         np.testing.assert_allclose(f32(out), want, atol=TOL[dtype], rtol=0)
 
 
+@pytest.mark.parametrize("case", ["ties", "over_sort_limit"])
+def test_prefill_request_order_covers_every_request(case):
+    """The tensor-core prefill takes requests longest first (batches up to
+    128; larger ones keep their order): with many equal lengths, and with a
+    batch past that limit, every output row must still be written once and
+    match the oracle (the output starts as NaN)."""
+    rng = np.random.default_rng(57)
+    if case == "ties":
+        kv_lens = [64, 130, 64, 1, 130, 64, 200, 1, 64, 130, 33, 64, 1, 200, 64, 33]
+    else:
+        kv_lens = rng.integers(1, 48, 140).tolist()
+    hq, hkv, d, dtype = 32, 8, 128, "bfloat16"
+    c = paged_case(58, kv_lens, hq, hkv, d, dtype=dtype)
+    q = po.round_to(rng.standard_normal((sum(kv_lens), hq, d), dtype=np.float32), dtype)
+    qo = np.concatenate([[0], np.cumsum(kv_lens)]).astype(np.int32)
+    want, _ = po.prefill_attention(q, qo, c["pool"], c["indptr"], c["indices"], c["last"], 16,
+                                   causal=True)
+    from mi_b200.prefill import BatchPrefillWithPagedKVCacheWrapper
+    w = BatchPrefillWithPagedKVCacheWrapper(torch.zeros(1 << 20, dtype=torch.uint8, device=DEV))
+    w.plan(i32(qo), i32(c["indptr"]), i32(c["indices"]), i32(c["last"]), hq, hkv, d, c["ps"],
+           causal=True, q_data_type=tdt(dtype))
+    qd = to_dev(q, dtype)
+    out = torch.full_like(qd, float("nan"))
+    w.run(qd, to_dev(c["pool"], dtype), out=out)
+    torch.cuda.synchronize()
+    w.check_status()
+    np.testing.assert_allclose(f32(out), want, atol=TOL[dtype], rtol=0)
+
+
 def test_prefill_qo_indptr_past_q_is_flagged_and_stays_in_bounds():
     """A qo_indptr that claims more query rows than q holds (request 1: 80
     rows, q has 30 of them) is clamped on the device and flagged
