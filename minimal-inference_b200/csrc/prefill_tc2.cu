@@ -227,8 +227,10 @@ __global__ void __launch_bounds__(kThreads2, 1)
         const int b = s_order[lo], ntq = tiles_pre[lo + 1] - tiles_pre[lo];
         const int rem = k - tiles_pre[lo] * p.hkv;
         rec.b = b;
-        rec.h = rem / ntq;
-        rec.t0 = (ntq - 1 - rem % ntq) * tq2;
+        // the request's query chunks heaviest (last) first, all KV heads of
+        // a chunk together
+        rec.h = rem % p.hkv;
+        rec.t0 = (ntq - 1 - rem / p.hkv) * tq2;
         rec.q_start = s_qo[b];
         rec.lq = s_qo[b + 1] - rec.q_start;
         rec.lk = s_lk[b];
