@@ -350,6 +350,9 @@ __global__ void __launch_bounds__(kThreads2, 1)
       const uint32_t idesc_qk = umma_idesc(fmt, false, kN, kM);
       const uint32_t idesc_qk_half = umma_idesc(fmt, false, kN / 2, kM);
       const uint32_t idesc_pv = umma_idesc(fmt, true, D, kM);
+      // tile B of the current item lies past its request's end (the request
+      // ends inside tile A): its products are not issued, its commits are
+      bool skip_b = false;
       // S_x = Q_x K^T of global tile t (K stage t % NK); a half tile (the
       // item's last, with at most kN / 2 visible keys) computes its first
       // kN / 2 columns only
@@ -357,7 +360,7 @@ __global__ void __launch_bounds__(kThreads2, 1)
         const uint32_t q_addr = smem_u32(smem + L::Q_OFF + x * L::Q_BYTES);
         const uint32_t k_addr = smem_u32(smem + L::K_OFF + (t % L::NK) * L::K_BYTES);
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
+        for (int kk = 0; kk < D / 16 && !(x == 1 && skip_b); ++kk) {
           const uint32_t off = (kk >> 2) * (kM * 128) + (kk & 3) * 32;
           const uint32_t koff = (kk >> 2) * (kN * 128) + (kk & 3) * 32;
           umma(tmem + L::S_COL + x * kN, umma_desc(q_addr + off, 16, 1024),
@@ -372,7 +375,7 @@ __global__ void __launch_bounds__(kThreads2, 1)
       auto issue_pv = [&](int t, int x, bool acc, bool half) {
         const uint32_t v_addr = smem_u32(smem + L::V_OFF + (t % L::NV) * L::V_BYTES);
 #pragma unroll
-        for (int kk = 0; kk < kN / 16; ++kk)
+        for (int kk = 0; kk < kN / 16 && !(x == 1 && skip_b); ++kk)
           if (!half || kk < kN / 32)
             umma_ts(tmem + L::O_COL + x * D, tmem + L::S_COL + x * kN + kk * 8,
                     umma_desc(v_addr + kk * 16 * 128, kN * 128, 1024), idesc_pv, acc || kk > 0);
@@ -389,6 +392,7 @@ __global__ void __launch_bounds__(kThreads2, 1)
         const int n = rec.n_tiles;
         if (n == 0) continue;
         const bool half_last = rec.last_keys <= kN / 2;  // the last tile is a half tile
+        skip_b = rec.lq - rec.t0 <= tq;
         // first products of the item: S_A(0), S_B(0)
         for (int x = 0; x < 2 && ok; ++x) {
           if (!mbar_wait_bounded(&q_full[x], oc & 1) ||
@@ -503,6 +507,13 @@ __global__ void __launch_bounds__(kThreads2, 1)
       for (int j = 0; j < rec.n_tiles; ++j, ++gt) {
         if (!__all_sync(0xffffffffu, mbar_wait_bounded(&s_full[x], gt & 1))) { ok = false; break; }
         tc_fence_after();
+        if (rows_tok == 0) {
+          // a tile past its request's end: no products were issued for it
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&p_full[x]);
+          continue;
+        }
         const int kbase = j * kN;
         // columns of S this tile computed: kN / 2 for a half tile (the
         // item's last, with at most kN / 2 visible keys)
