@@ -356,15 +356,21 @@ __global__ void __launch_bounds__(kThreads2, 1)
       // S_x = Q_x K^T of global tile t (K stage t % NK); a half tile (the
       // item's last, with at most kN / 2 visible keys) computes its first
       // kN / 2 columns only
+      // descriptors of the stage bases; a descriptor's start field is the
+      // address / 16 (shared memory < 256 KB), so an offset adds offset / 16
+      const uint64_t qdesc0 = umma_desc(smem_u32(smem + L::Q_OFF), 16, 1024);
+      const uint64_t kdesc0 = umma_desc(smem_u32(smem + L::K_OFF), 16, 1024);
+      const uint64_t vdesc0 = umma_desc(smem_u32(smem + L::V_OFF), kN * 128, 1024);
       auto issue_qk = [&](int t, int x, bool half) {
-        const uint32_t q_addr = smem_u32(smem + L::Q_OFF + x * L::Q_BYTES);
-        const uint32_t k_addr = smem_u32(smem + L::K_OFF + (t % L::NK) * L::K_BYTES);
+        const uint64_t qd = qdesc0 + ((x * L::Q_BYTES) >> 4);
+        const uint64_t kd = kdesc0 + (((t % L::NK) * L::K_BYTES) >> 4);
+        const uint32_t id = half ? idesc_qk_half : idesc_qk;
+        const uint32_t d_col = tmem + L::S_COL + x * kN;
 #pragma unroll
         for (int kk = 0; kk < D / 16 && !(x == 1 && skip_b); ++kk) {
           const uint32_t off = (kk >> 2) * (kM * 128) + (kk & 3) * 32;
           const uint32_t koff = (kk >> 2) * (kN * 128) + (kk & 3) * 32;
-          umma(tmem + L::S_COL + x * kN, umma_desc(q_addr + off, 16, 1024),
-               umma_desc(k_addr + koff, 16, 1024), half ? idesc_qk_half : idesc_qk, kk > 0);
+          umma(d_col, qd + (off >> 4), kd + (koff >> 4), id, kk > 0);
         }
         umma_commit(&s_full[x]);
       };
@@ -373,12 +379,12 @@ __global__ void __launch_bounds__(kThreads2, 1)
       // bytes apart, 8-token groups 1 KB apart; a half tile's first kN / 2
       // keys only
       auto issue_pv = [&](int t, int x, bool acc, bool half) {
-        const uint32_t v_addr = smem_u32(smem + L::V_OFF + (t % L::NV) * L::V_BYTES);
+        const uint64_t vd = vdesc0 + (((t % L::NV) * L::V_BYTES) >> 4);
+        const uint32_t o_col = tmem + L::O_COL + x * D, p_col = tmem + L::S_COL + x * kN;
 #pragma unroll
         for (int kk = 0; kk < kN / 16 && !(x == 1 && skip_b); ++kk)
           if (!half || kk < kN / 32)
-            umma_ts(tmem + L::O_COL + x * D, tmem + L::S_COL + x * kN + kk * 8,
-                    umma_desc(v_addr + kk * 16 * 128, kN * 128, 1024), idesc_pv, acc || kk > 0);
+            umma_ts(o_col, p_col + kk * 8, vd + ((kk * 16 * 128) >> 4), idesc_pv, acc || kk > 0);
         umma_commit(&pv_done[x]);
       };
       int gt = 0, oc = 0;
