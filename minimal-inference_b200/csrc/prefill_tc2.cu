@@ -21,12 +21,12 @@
 //               one tile's softmax warps work on S, the pipe works for the
 //               other tile;
 //   warps 2-5   softmax of tile A, warps 6-9 softmax of tile B: thread = TMEM
-//               lane = packed row, the whole 128-key row of S. After an
-//               item's first tile in one pass over TMEM against the running
-//               max (exp2, row sum, 16-bit P written over the S columns it
-//               came from); the first tile, and any tile whose max grows by
-//               more than 2^8, in two (row max first); O rescaled in TMEM
-//               only then;
+//               lane = packed row, the whole 128-key row of S in one pass
+//               over TMEM against the running max (in an item's first tile,
+//               the max of its first 32 keys): exp2, row sum, 16-bit P
+//               written over the S columns it came from; a tile whose max
+//               exceeds that by more than 2^8 is redone in two passes (row
+//               max first), with O rescaled in TMEM only then;
 //   warps 10-13 epilogue: normalise a finished item's O_A and O_B and store
 //               them, releasing each O buffer as soon as it is read.
 // An item's last tile is a half tile when at most 64 of its keys are visible
@@ -536,12 +536,27 @@ __global__ void __launch_bounds__(kThreads2, 1)
         };
         float corr = 1.f, sum = 0.f, m_new = m;
         bool fast = false;
-        if (j > 0) {
-          // one pass against the running max m: P = 2^(s * scale - m), right
-          // unless a key of this tile exceeds m + kRescaleLog2 (then the two
-          // passes below redo the tile). The row max and the row sum run in
-          // four independent chains each, off the exponentials' path.
-          const float ms = m == -INFINITY ? 0.f : m;  // a row with no key yet
+        // the max the one pass works against: the running max, or in an
+        // item's first tile the row max of its first 32 keys (key 0 is
+        // visible to every row that sees any key)
+        float mb = m;
+        if (j == 0) {
+          float sv[32];
+          load_chunk(0, sv);
+          float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+          for (int i = 0; i < 32; i += 4) {
+            mx0 = max3f(mx0, sv[i], sv[i + 1]);
+            mx1 = max3f(mx1, sv[i + 2], sv[i + 3]);
+          }
+          mb = fmaxf(mx0, mx1) * p.scale_log2;
+        }
+        {
+          // one pass against mb: P = 2^(s * scale - mb), right unless a key
+          // of this tile exceeds mb + kRescaleLog2 (then the two passes
+          // below redo the tile). The row max and the row sum run in four
+          // independent chains each, off the exponentials' path.
+          const float ms = mb == -INFINITY ? 0.f : mb;  // a row with no key yet
           float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
           float sm[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll 1
@@ -561,7 +576,8 @@ __global__ void __launch_bounds__(kThreads2, 1)
           }
           const float mt = max3f(mx[0], mx[1], fmaxf(mx[2], mx[3])) * p.scale_log2;
           sum = (sm[0] + sm[1]) + (sm[2] + sm[3]);
-          fast = __all_sync(0xffffffffu, !(mt > m + kRescaleLog2));
+          fast = __all_sync(0xffffffffu, !(mt > mb + kRescaleLog2));
+          m_new = mb;  // (m itself after the first tile; O holds nothing before it)
         }
         if (!fast) {
           // pass 1: the row max over the tile's keys (raw scores; the scale
