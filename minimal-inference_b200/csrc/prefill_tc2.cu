@@ -540,29 +540,28 @@ __global__ void __launch_bounds__(kThreads2, 1)
         // item's first tile the row max of its first 32 keys (key 0 is
         // visible to every row that sees any key)
         float mb = m;
-        if (j == 0) {
-          float sv[32];
-          load_chunk(0, sv);
-          float mx0 = -INFINITY, mx1 = -INFINITY;
-#pragma unroll
-          for (int i = 0; i < 32; i += 4) {
-            mx0 = max3f(mx0, sv[i], sv[i + 1]);
-            mx1 = max3f(mx1, sv[i + 2], sv[i + 3]);
-          }
-          mb = fmaxf(mx0, mx1) * p.scale_log2;
-        }
         {
           // one pass against mb: P = 2^(s * scale - mb), right unless a key
           // of this tile exceeds mb + kRescaleLog2 (then the two passes
           // below redo the tile). The row max and the row sum run in four
           // independent chains each, off the exponentials' path.
-          const float ms = mb == -INFINITY ? 0.f : mb;  // a row with no key yet
+          float ms = mb == -INFINITY ? 0.f : mb;  // a row with no key yet
           float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
           float sm[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll 1
           for (int c = 0; c < ncol / 32; ++c) {
             float sv[32];
             load_chunk(c, sv);
+            if (j == 0 && c == 0) {  // an item's first tile: mb from its first chunk
+              float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+              for (int i = 0; i < 32; i += 4) {
+                mx0 = max3f(mx0, sv[i], sv[i + 1]);
+                mx1 = max3f(mx1, sv[i + 2], sv[i + 3]);
+              }
+              mb = fmaxf(mx0, mx1) * p.scale_log2;
+              ms = mb == -INFINITY ? 0.f : mb;
+            }
             uint32_t pk[16];
 #pragma unroll
             for (int i = 0; i < 32; i += 2) {
