@@ -399,10 +399,14 @@ __global__ void __launch_bounds__(kThreads2, 1)
         if (n == 0) continue;
         const bool half_last = rec.last_keys <= kN / 2;  // the last tile is a half tile
         skip_b = rec.lq - rec.t0 <= tq;
-        // first products of the item: S_A(0), S_B(0)
+        // first products of the item: S_A(0), S_B(0), each once the previous
+        // item's last P_x V has completed. S_x is written over P_x, which
+        // that product reads from TMEM, and products into different TMEM
+        // accumulators are not ordered by their issue order.
         for (int x = 0; x < 2 && ok; ++x) {
           if (!mbar_wait_bounded(&q_full[x], oc & 1) ||
-              (x == 0 && !mbar_wait_bounded(&k_full[gt % L::NK], (gt / L::NK) & 1))) {
+              (x == 0 && !mbar_wait_bounded(&k_full[gt % L::NK], (gt / L::NK) & 1)) ||
+              (gt >= 1 && !mbar_wait_bounded(&pv_done[x], (gt - 1) & 1))) {
             ok = false;
             break;
           }

@@ -18,7 +18,10 @@ synchronisation steps in program order:
 It raises ``AssertionError`` on a deadlock (nothing can move), on a wait
 that passes on another completion than the one it names (phase aliasing:
 a parity wait cannot tell completion ``n`` from ``n - 1`` or ``n + 2``) and
-on arrivals beyond a barrier's count.
+on arrivals beyond a barrier's count. ``hazards`` maps a product tag to the
+tags of products it overwrites the operands of (products on different
+accumulators need not run in issue order): issuing it while one of those is
+still in flight raises too.
 """
 from __future__ import annotations
 
@@ -37,7 +40,8 @@ class Bar:
             self.done += 1
 
 
-def run(bars: dict, roles: dict, seed: int, max_steps: int = 10 ** 6) -> None:
+def run(bars: dict, roles: dict, seed: int, max_steps: int = 10 ** 6,
+        hazards: dict | None = None) -> None:
     rnd = random.Random(seed)
     pending = []     # barriers with an asynchronous copy in flight
     products = {}    # per issuing role, in order: ("mma", tag) / ("commit", bar)
@@ -76,7 +80,11 @@ def run(bars: dict, roles: dict, seed: int, max_steps: int = 10 ** 6) -> None:
                 elif kind == "tma":
                     pending.append(act[1])
                 else:
-                    products.setdefault(name, []).append(act)
+                    queue = products.setdefault(name, [])
+                    if kind == "mma" and hazards:
+                        busy = [a[1] for a in queue if a[0] == "mma" and a[1] in hazards.get(act[1], ())]
+                        assert not busy, f"{name}: {act[1]} issued while {busy[0]} is in flight"
+                    queue.append(act)
                 act, progress = None, True
                 if rnd.random() < 0.3:
                     break

@@ -103,6 +103,8 @@ def _model(items, plant=None):
                 yield ("wait", f"q_full{x}", oc)
                 if x == 0:
                     yield ("wait", f"k_full{gt % NK}", gt // NK)
+                if gt >= 1 and plant != "no_pv_wait_at_item_start":
+                    yield ("wait", f"pv_done{x}", gt - 1)
                 yield ("mma", f"S{x}")
                 yield ("commit", f"s_full{x}")
                 issued = True
@@ -189,12 +191,33 @@ def _items(rnd, count):
     return [rnd.choice([0, 1, 1, 2, 3, 4, 7]) for _ in range(count)]
 
 
+# S_x is written over P_x, which the tile's P V reads from TMEM; a P V and an
+# S accumulate into different TMEM columns, so nothing orders them but the
+# pv_done wait
+HAZARDS = {"S0": {"PV0"}, "S1": {"PV1"}}
+
+
 @pytest.mark.parametrize("seed", range(60))
 def test_random_item_sequences_finish(seed):
     rnd = random.Random(seed)
     items = _items(rnd, rnd.randrange(0, 9))
     bars, roles = _model(items)
-    run(bars, roles, seed)
+    run(bars, roles, seed, hazards=HAZARDS)
+
+
+def test_a_first_s_without_the_pv_wait_is_caught():
+    """An item's first S_x issued without waiting for the previous item's
+    last P_x V: on some schedule that P V is still in flight when S_x
+    overwrites P_x."""
+    caught = 0
+    for seed in range(200):
+        bars, roles = _model([2, 1, 3, 1], plant="no_pv_wait_at_item_start")
+        try:
+            run(bars, roles, seed, hazards=HAZARDS)
+        except AssertionError as e:
+            assert "in flight" in str(e)
+            caught += 1
+    assert caught > 0
 
 
 def test_a_slot_wait_on_a_per_item_barrier_is_caught():
