@@ -206,7 +206,9 @@ __global__ void __launch_bounds__(kThreads2, 1)
 
   if (warp == 0) {
     // ============================ producer ==================================
-    const uint64_t pol_q = evict_last_policy(), pol_kv = evict_first_policy();
+    // a Q tile is read by one work item; a request's K/V tiles by every
+    // query chunk of the request: K/V are the lines worth keeping in L2
+    const uint64_t pol_q = evict_first_policy(), pol_kv = evict_last_policy();
     int gt = 0, qc = 0;
     int k_ahead = -1;  // lane 0: the next item's index, taken while this item's last V tiles go out
     for (int it = 0; ok; ++it) {

@@ -59,8 +59,10 @@ __device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, i
       : "memory");
 }
 
-// The KV stream is read once: evict-first keeps it from pushing partials and
-// metadata out of L2. Queries are reused by every KV tile: evict-last.
+// L2 eviction priorities for TMA loads. Decode reads its KV stream once
+// (evict-first, so it does not push partials and metadata out of L2) and
+// reuses the queries for every KV tile (evict-last); prefill the other way
+// round.
 __device__ __forceinline__ uint64_t evict_first_policy() {
   uint64_t pol;
   asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
