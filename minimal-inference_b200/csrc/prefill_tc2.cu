@@ -319,18 +319,19 @@ __global__ void __launch_bounds__(kThreads2, 1)
         }
         return true;
       };
-      // K runs one tile ahead of V: K0, K1, V0, K2, V1, ..., V(n-1)
+      // in the order the tensor core uses them, which is also the order
+      // their stages free up: K0, V0, K1, V1, ..., K(n-1), V(n-1)
       int pg_prev = -1;
       for (int j = 0; j < rec.n_tiles && ok; ++j, ++gt) {
+        if (j > 0 && !issue(j - 1, gt - 1, 1, pg_prev)) ok = false;
         if (j > 0 && (j & 3) == 0) {  // next window of page ids
           pw = pwn;
           pwn = load_win((j >> 2) + 1);
         }
         const int pg = __shfl_sync(0xffffffffu, pw, ((j & 3) << 3) + min(lane / DH, 7));
-        if (!issue(j, gt, 0, pg)) ok = false;
+        if (ok && !issue(j, gt, 0, pg)) ok = false;
         if (ok && j + 1 == rec.n_tiles && lane == 0 && p.ctr)
-          k_ahead = static_cast<int>(atomicAdd(p.ctr, 1u));  // used after the V tiles below
-        if (ok && j > 0 && !issue(j - 1, gt - 1, 1, pg_prev)) ok = false;
+          k_ahead = static_cast<int>(atomicAdd(p.ctr, 1u));  // used after the V tile below
         pg_prev = pg;
       }
       if (ok && !issue(rec.n_tiles - 1, gt - 1, 1, pg_prev)) ok = false;

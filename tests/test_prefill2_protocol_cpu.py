@@ -72,10 +72,10 @@ def _model(items, plant=None):
                 if g >= nst:
                     yield ("wait", f"{kind}_empty{g % nst}", g // nst - 1)
                 yield ("tma", f"{kind}_full{g % nst}")
-            for j in range(n):                      # K0, K1, V0, K2, V1, ..., V(n-1)
-                yield from issue(gt, 0)
+            for j in range(n):                      # K0, V0, K1, V1, ..., K(n-1), V(n-1)
                 if j > 0:
                     yield from issue(gt - 1, 1)
+                yield from issue(gt, 0)
                 gt += 1
             yield from issue(gt - 1, 1)
         # drain: the last copies have landed
