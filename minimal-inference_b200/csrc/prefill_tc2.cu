@@ -24,9 +24,11 @@
 //               lane = packed row, the whole 128-key row of S in one pass
 //               over TMEM against the running max (in an item's first tile,
 //               the max of its first 32 keys): exp2, row sum, 16-bit P
-//               written over the S columns it came from; a tile whose max
-//               exceeds that by more than 2^8 is redone in two passes (row
-//               max first), with O rescaled in TMEM only then;
+//               written over S columns already read, chunk by chunk; from
+//               the first chunk with a key more than 2^8 above that max the
+//               tile takes two passes (row max first) against a new max,
+//               the P already written is rebased, and O is rescaled in TMEM
+//               only then;
 //   warps 10-13 epilogue: normalise a finished item's O_A and O_B and store
 //               them, releasing each O buffer as soon as it is read.
 // An item's last tile is a half tile when at most 64 of its keys are visible
@@ -542,21 +544,25 @@ __global__ void __launch_bounds__(kThreads2, 1)
           }
         };
         float corr = 1.f, sum = 0.f, m_new = m;
-        bool fast = false;
         // the max the one pass works against: the running max, or in an
         // item's first tile the row max of its first 32 keys (key 0 is
         // visible to every row that sees any key)
         float mb = m;
         {
-          // one pass against mb: P = 2^(s * scale - mb), right unless a key
-          // of this tile exceeds mb + kRescaleLog2 (then the two passes
-          // below redo the tile). The row max and the row sum run in four
-          // independent chains each, off the exponentials' path.
+          // one pass against mb: P = 2^(s * scale - mb) chunk by chunk, each
+          // chunk's P written over S columns already read. A chunk with a
+          // key above mb + kRescaleLog2 (in a row of the warp) is not
+          // written: from it on the tile takes two passes against a new
+          // max, its S and the later chunks' being still in TMEM, and the P
+          // already written (at most 2^kRescaleLog2, so it fits the 16-bit
+          // type) is rebased. Row maxima and sums run in four independent
+          // chains each, off the exponentials' path.
           float ms = mb == -INFINITY ? 0.f : mb;  // a row with no key yet
-          float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
           float sm[4] = {0.f, 0.f, 0.f, 0.f};
+          float cmax = -INFINITY;  // raw row max of the chunk the loop stopped at
+          int c = 0;
 #pragma unroll 1
-          for (int c = 0; c < ncol / 32; ++c) {
+          for (; c < ncol / 32; ++c) {
             float sv[32];
             load_chunk(c, sv);
             if (j == 0 && c == 0) {  // an item's first tile: mb from its first chunk
@@ -569,54 +575,73 @@ __global__ void __launch_bounds__(kThreads2, 1)
               mb = fmaxf(mx0, mx1) * p.scale_log2;
               ms = mb == -INFINITY ? 0.f : mb;
             }
+            float cm[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+            float cs[4] = {0.f, 0.f, 0.f, 0.f};
             uint32_t pk[16];
 #pragma unroll
             for (int i = 0; i < 32; i += 2) {
-              mx[(i >> 1) & 3] = max3f(mx[(i >> 1) & 3], sv[i], sv[i + 1]);
+              cm[(i >> 1) & 3] = max3f(cm[(i >> 1) & 3], sv[i], sv[i + 1]);
               const float p0 = fast_exp2(fmaf(sv[i], p.scale_log2, -ms));  // 2^-inf = 0
               const float p1 = fast_exp2(fmaf(sv[i + 1], p.scale_log2, -ms));
-              sm[(i >> 1) & 3] += p0 + p1;
+              cs[(i >> 1) & 3] += p0 + p1;
               pk[i >> 1] = Pack2<T>::run(p0, p1);
             }
+            cmax = max3f(cm[0], cm[1], fmaxf(cm[2], cm[3]));
+            if (__any_sync(0xffffffffu, cmax * p.scale_log2 > mb + kRescaleLog2)) break;
             tmem_st16(tmem_s + c * 16, pk);  // columns [16 c, 16 c + 16): read already
+#pragma unroll
+            for (int k = 0; k < 4; ++k) sm[k] += cs[k];
           }
-          const float mt = max3f(mx[0], mx[1], fmaxf(mx[2], mx[3])) * p.scale_log2;
           sum = (sm[0] + sm[1]) + (sm[2] + sm[3]);
-          fast = __all_sync(0xffffffffu, !(mt > mb + kRescaleLog2));
           m_new = mb;  // (m itself after the first tile; O holds nothing before it)
-        }
-        if (!fast) {
-          // pass 1: the row max over the tile's keys (raw scores; the scale
-          // is folded into the exponent's FMA)
-          float mt = -INFINITY;
+          if (c < ncol / 32) {
+            // pass 1 over chunk c and the rest: their row max (raw scores;
+            // scale_log2 > 0, so the max commutes with it)
+            float mt = cmax;
 #pragma unroll 1
-          for (int c = 0; c < ncol / 32; ++c) {
-            float sv[32];
-            load_chunk(c, sv);
+            for (int c2 = c + 1; c2 < ncol / 32; ++c2) {
+              float sv[32];
+              load_chunk(c2, sv);
 #pragma unroll
-            for (int i = 0; i < 32; ++i) mt = fmaxf(mt, sv[i]);
-          }
-          mt *= p.scale_log2;  // scale_log2 > 0: the max commutes with it
-          // keep the old max unless this tile's exceeds it by > kRescaleLog2
-          m_new = (mt > m + kRescaleLog2 || m == -INFINITY) ? fmaxf(m, mt) : m;
-          const float ms = m_new == -INFINITY ? 0.f : m_new;
-          corr = m == m_new ? 1.f : fast_exp2(m - ms);
-          // pass 2: P = 2^(s * scale - m) as 16-bit pairs over the S columns
-          // already read (chunk c's P lands in columns [16 c, 16 c + 16))
-          sum = 0.f;
-#pragma unroll 1
-          for (int c = 0; c < ncol / 32; ++c) {
-            float sv[32];
-            load_chunk(c, sv);
-            uint32_t pk[16];
-#pragma unroll
-            for (int i = 0; i < 32; i += 2) {
-              const float p0 = fast_exp2(fmaf(sv[i], p.scale_log2, -ms));
-              const float p1 = fast_exp2(fmaf(sv[i + 1], p.scale_log2, -ms));
-              sum += p0 + p1;
-              pk[i >> 1] = Pack2<T>::run(p0, p1);
+              for (int i = 0; i < 32; ++i) mt = fmaxf(mt, sv[i]);
             }
-            tmem_st16(tmem_s + c * 16, pk);
+            mt *= p.scale_log2;
+            // keep mb unless they exceed it by more than kRescaleLog2
+            m_new = (mt > mb + kRescaleLog2 || mb == -INFINITY) ? fmaxf(mb, mt) : mb;
+            const float ms2 = m_new == -INFINITY ? 0.f : m_new;
+            corr = m_new == mb ? 1.f : fast_exp2(mb - ms2);
+            sum *= corr;
+            // the P written for the chunks before c, rebased on m_new
+            if (c > 0 && __any_sync(0xffffffffu, corr != 1.f)) {
+#pragma unroll 1
+              for (int c2 = 0; c2 < c; ++c2) {
+                float pw[16];
+                tmem_ld16(tmem_s + c2 * 16, pw);
+                tmem_wait_ld();
+                uint32_t pk[16];
+#pragma unroll
+                for (int i = 0; i < 16; ++i) {
+                  const float2 f = Unpack2<T>::run(__float_as_uint(pw[i]));
+                  pk[i] = Pack2<T>::run(f.x * corr, f.y * corr);
+                }
+                tmem_st16(tmem_s + c2 * 16, pk);
+              }
+            }
+            // pass 2: P of chunk c and the rest against m_new
+#pragma unroll 1
+            for (int c2 = c; c2 < ncol / 32; ++c2) {
+              float sv[32];
+              load_chunk(c2, sv);
+              uint32_t pk[16];
+#pragma unroll
+              for (int i = 0; i < 32; i += 2) {
+                const float p0 = fast_exp2(fmaf(sv[i], p.scale_log2, -ms2));
+                const float p1 = fast_exp2(fmaf(sv[i + 1], p.scale_log2, -ms2));
+                sum += p0 + p1;
+                pk[i >> 1] = Pack2<T>::run(p0, p1);
+              }
+              tmem_st16(tmem_s + c2 * 16, pk);
+            }
           }
         }
         l = l * corr + sum;

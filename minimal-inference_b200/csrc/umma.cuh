@@ -131,6 +131,19 @@ template <> struct Pack2<__half> {
   }
 };
 
+// The two fp32 values of a Pack2 word (low half first).
+template <typename T> struct Unpack2;
+template <> struct Unpack2<__nv_bfloat16> {
+  __device__ __forceinline__ static float2 run(uint32_t u) {
+    return __bfloat1622float2(*reinterpret_cast<__nv_bfloat162 *>(&u));
+  }
+};
+template <> struct Unpack2<__half> {
+  __device__ __forceinline__ static float2 run(uint32_t u) {
+    return __half22float2(*reinterpret_cast<__half2 *>(&u));
+  }
+};
+
 // 16 consecutive fp32 TMEM columns of this thread's lane.
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float *v) {
   uint32_t r[16];

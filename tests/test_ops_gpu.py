@@ -425,6 +425,35 @@ def test_prefill_ragged(dtype, hq, hkv, d, causal):
     np.testing.assert_allclose(lse, wlse, atol=max(TOL[dtype], 1e-3), rtol=0)
 
 
+@pytest.mark.parametrize("dtype", ["bfloat16", "float16"])
+def test_prefill_score_spikes_take_the_rescale_path(dtype):
+    """Keys that outscore every earlier key of their rows by far more than
+    2^8 (in exp2 units), in a first K/V tile's later chunks (past the first
+    32 keys, whose max seeds an item's one pass) and in later tiles (past
+    the running max): the softmax redoes those tiles in two passes and
+    rescales O in TMEM. The result still matches the oracle."""
+    hq, hkv, d = 32, 8, 128
+    lens = [600, 260]
+    c = paged_case(61, lens, hq, hkv, d, dtype=dtype)
+    rng = np.random.default_rng(62)
+    u = rng.standard_normal(d).astype(np.float32)
+    u /= np.linalg.norm(u)
+    pool = c["pool"].copy()
+    # q . spike = (3 + N(0,1)) * 60: about 23 in exp2 units after the
+    # 1/sqrt(d) scale, against about 4 for the largest ordinary key
+    for r, spikes in enumerate([[100, 300, 301, 520], [90, 200]]):
+        for pos in spikes:
+            page = c["tables"][r][pos // c["ps"]]
+            pool[page, 0, pos % c["ps"]] = po.round_to(np.tile(60.0 * u, (hkv, 1)), dtype)
+    c["pool"] = pool
+    q = po.round_to(rng.standard_normal((sum(lens), hq, d)).astype(np.float32) + 3.0 * u, dtype)
+    qo, out, lse = run_prefill(c, lens, q)
+    want, wlse = po.prefill_attention(q, qo, c["pool"], c["indptr"], c["indices"], c["last"],
+                                      16, causal=True)
+    np.testing.assert_allclose(out, want, atol=TOL[dtype], rtol=0)
+    np.testing.assert_allclose(lse, wlse, atol=2e-2, rtol=0)
+
+
 @pytest.mark.parametrize("ws_bytes", [1 << 20, 16])
 def test_prefill_repeated_calls_share_workspace(ws_bytes):
     """The persistent tensor-core prefill hands out work items through counters
