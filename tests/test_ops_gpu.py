@@ -237,6 +237,29 @@ def test_decode_batch_sizes(batch):
     check_decode(paged_case(12 + batch, lens, 32, 8, 128))
 
 
+@pytest.mark.parametrize("dtype", ["bfloat16", "float16"])
+def test_decode_score_spikes(dtype):
+    """Keys scoring far above every other key of their request (about 23 in
+    exp2 units after the scale, against about 4), early, mid-tile and deep
+    into long contexts: the running max jumps inside a 16-key tile, across
+    tiles and across the split-K runs merged at the end."""
+    hq, hkv, d = 32, 8, 128
+    lens = [700, 3000, 40, 1]
+    c = paged_case(71, lens, hq, hkv, d, dtype=dtype)
+    rng = np.random.default_rng(72)
+    u = rng.standard_normal(d).astype(np.float32)
+    u /= np.linalg.norm(u)
+    pool = c["pool"].copy()
+    for r, spikes in enumerate([[3, 301, 650], [17, 1800, 1801, 2999], [39], []]):
+        for pos in spikes:
+            page = c["tables"][r][pos // c["ps"]]
+            pool[page, 0, pos % c["ps"]] = po.round_to(np.tile(60.0 * u, (hkv, 1)), dtype)
+    c["pool"] = pool
+    c["q"] = po.round_to(rng.standard_normal((len(lens), hq, d)).astype(np.float32) + 3.0 * u,
+                         dtype)
+    check_decode(c)
+
+
 def test_decode_split_k_long_contexts():
     """Few long requests: many chunks per (request, head), merged on device."""
     check_decode(paged_case(13, [4096, 4095, 1, 2049], 32, 8, 128))
