@@ -456,15 +456,16 @@ def test_prefill_score_spikes_take_the_rescale_path(dtype):
     the running max): the softmax redoes those tiles in two passes and
     rescales O in TMEM. The result still matches the oracle."""
     hq, hkv, d = 32, 8, 128
-    lens = [600, 260]
+    lens = [600, 260, 300]
     c = paged_case(61, lens, hq, hkv, d, dtype=dtype)
     rng = np.random.default_rng(62)
     u = rng.standard_normal(d).astype(np.float32)
     u /= np.linalg.norm(u)
     pool = c["pool"].copy()
     # q . spike = (3 + N(0,1)) * 60: about 23 in exp2 units after the
-    # 1/sqrt(d) scale, against about 4 for the largest ordinary key
-    for r, spikes in enumerate([[100, 300, 301, 520], [90, 200]]):
+    # 1/sqrt(d) scale, against about 4 for the largest ordinary key; the
+    # third request's one spike opens its second K/V tile
+    for r, spikes in enumerate([[100, 300, 301, 520], [90, 200], [130]]):
         for pos in spikes:
             page = c["tables"][r][pos // c["ps"]]
             pool[page, 0, pos % c["ps"]] = po.round_to(np.tile(60.0 * u, (hkv, 1)), dtype)
