@@ -12,7 +12,9 @@ synchronisation steps in program order:
 * ``("commit", bar)``     an arrival on ``bar`` once every product the same
                           role issued before it has completed (each role's
                           products complete in its issue order; two roles'
-                          products in any interleaving).
+                          products in any interleaving), and
+* ``("tmem", region)``    a read or write of a TMEM region by the role's own
+                          threads.
 
 ``run`` interleaves the roles and the asynchronous completions at random.
 It raises ``AssertionError`` on a deadlock (nothing can move), on a wait
@@ -21,7 +23,9 @@ a parity wait cannot tell completion ``n`` from ``n - 1`` or ``n + 2``) and
 on arrivals beyond a barrier's count. ``hazards`` maps a product tag to the
 tags of products it overwrites the operands of (products on different
 accumulators need not run in issue order): issuing it while one of those is
-still in flight raises too.
+still in flight raises too, and ``tmem_hazards`` maps a TMEM region to the
+tags of the products that write it: a ``tmem`` access to it while one of
+those is in flight (any role's) raises.
 """
 from __future__ import annotations
 
@@ -41,7 +45,7 @@ class Bar:
 
 
 def run(bars: dict, roles: dict, seed: int, max_steps: int = 10 ** 6,
-        hazards: dict | None = None) -> None:
+        hazards: dict | None = None, tmem_hazards: dict | None = None) -> None:
     rnd = random.Random(seed)
     pending = []     # barriers with an asynchronous copy in flight
     products = {}    # per issuing role, in order: ("mma", tag) / ("commit", bar)
@@ -75,7 +79,12 @@ def run(bars: dict, roles: dict, seed: int, max_steps: int = 10 ** 6,
                     assert bar.done <= n, (
                         f"{name}: wait on {act[1]} for completion {n} aliased at {bar.done}")
                     break
-                if kind == "arrive":
+                if kind == "tmem":
+                    writers = (tmem_hazards or {}).get(act[1], ())
+                    busy = [a[1] for q in products.values() for a in q
+                            if a[0] == "mma" and a[1] in writers]
+                    assert not busy, f"{name}: {act[1]} accessed while {busy[0]} is in flight"
+                elif kind == "arrive":
                     bars[act[1]].arrive()
                 elif kind == "tma":
                     pending.append(act[1])

@@ -157,8 +157,10 @@ def _model(items, plant=None):
                 break
             if n == 0:
                 continue
-            for _ in range(n):
+            for j in range(n):
                 yield ("wait", f"s_full{x}", gt)
+                if j > 0:
+                    yield ("tmem", f"O{x}")          # O rescaled when the row max moved
                 yield ("arrive", f"p_full{x}")
                 gt += 1
             hs = oc & 1
@@ -178,7 +180,9 @@ def _model(items, plant=None):
                 yield ("wait", f"l_ready{slot * 2 + x}", oc >> 1)
                 if x == 0 and oc == n_keyed:
                     return                           # the end record
-                yield ("wait", f"o_full{x}", oc)
+                if plant != "epilogue_reads_o_early":
+                    yield ("wait", f"o_full{x}", oc)
+                yield ("tmem", f"O{x}")                  # O read for the output
                 yield ("arrive", f"o_free{x}")
                 yield ("arrive", f"h_free{slot * 2 + x}")
 
@@ -195,6 +199,9 @@ def _items(rnd, count):
 # S accumulate into different TMEM columns, so nothing orders them but the
 # pv_done wait
 HAZARDS = {"S0": {"PV0"}, "S1": {"PV1"}}
+# O_x is written by the tile's P V products and read or rescaled by the
+# softmax and epilogue warps
+TMEM_HAZARDS = {"O0": {"PV0"}, "O1": {"PV1"}}
 
 
 @pytest.mark.parametrize("seed", range(60))
@@ -202,7 +209,20 @@ def test_random_item_sequences_finish(seed):
     rnd = random.Random(seed)
     items = _items(rnd, rnd.randrange(0, 9))
     bars, roles = _model(items)
-    run(bars, roles, seed, hazards=HAZARDS)
+    run(bars, roles, seed, hazards=HAZARDS, tmem_hazards=TMEM_HAZARDS)
+
+
+def test_an_epilogue_read_before_o_full_is_caught():
+    """The epilogue reading O_x without waiting for the item's last P_x V:
+    on some schedule that product is still writing O_x."""
+    caught = 0
+    for seed in range(200):
+        bars, roles = _model([2, 1, 3], plant="epilogue_reads_o_early")
+        try:
+            run(bars, roles, seed, hazards=HAZARDS, tmem_hazards=TMEM_HAZARDS)
+        except AssertionError as e:
+            caught += "accessed while" in str(e)
+    assert caught > 0
 
 
 def test_a_first_s_without_the_pv_wait_is_caught():
@@ -213,7 +233,7 @@ def test_a_first_s_without_the_pv_wait_is_caught():
     for seed in range(200):
         bars, roles = _model([2, 1, 3, 1], plant="no_pv_wait_at_item_start")
         try:
-            run(bars, roles, seed, hazards=HAZARDS)
+            run(bars, roles, seed, hazards=HAZARDS, tmem_hazards=TMEM_HAZARDS)
         except AssertionError as e:
             assert "in flight" in str(e)
             caught += 1
